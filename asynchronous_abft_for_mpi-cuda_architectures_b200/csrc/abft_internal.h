@@ -1,0 +1,119 @@
+// Internal declarations shared by the kernels, the C ABI and the pipeline.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+#include <vector>
+
+namespace abft {
+
+constexpr int kThreads = 256;    // threads of the verify / localise CTAs
+constexpr int kWarps = kThreads / 32;
+constexpr int kGroupCols = 128;  // columns per verify CTA: 32 lanes x 4 columns
+constexpr int kMaxChunks = 64;   // row chunks per column group (verify partials)
+
+// One row-chunk partial of a column: double sum, float sum of |x| and the
+// smallest (|x| bits - 1) (unsigned; 0xffffffff when every term is zero).
+struct ColPartial {
+    double s;
+    float t;
+    uint32_t mbm1;
+};
+
+// Per-fragment decision record (the reference's dErrCol[f] / dRowDiff[f],
+// plus the located row).
+struct FragRecord {
+    int errcol;
+    int errrow;
+    double rowdiff;
+};
+
+struct DecisionLog {
+    int errcol;
+    int errrow;
+    double rowdiff;
+};
+
+struct InjectLog {
+    int frag, row, col, bit;
+    float before, after;
+};
+
+struct PendingFix {
+    int it, f, er, ec, injected, off;
+    double rowdiff;
+    double tau;
+    float c_fault;
+    float pad;
+};
+
+struct Counters {
+    int cm[4];       // TP, TN, FP, FN
+    int n_restored;
+    int n_pending;
+    int pad[2];
+};
+
+// Device-side workspace pointers (plain struct, passed by value to kernels).
+struct WsDev {
+    double* colSumA;   // [K]
+    double* expRow;    // [N_b]  absolute column index
+    double* rowSumB;   // [F][K]
+    double* expCol;    // [F][M_b]
+    FragRecord* rec;   // [F]
+    Counters* ctr;
+    ColPartial* vpart; // [kMaxChunks][nfpad]
+    double* vact;      // [nfpad]
+    double* vd;
+    double* vw;
+    int* vcnt;         // [groups_max + 1]
+    double* lact;      // [M_b]
+    double* ld;
+    double* lw;
+    int* lcnt;         // [1]
+    DecisionLog* dlog; // [max_iters][F]
+    InjectLog* ilog;   // [max_iters]
+    PendingFix* pend;  // [max_iters * F]
+};
+
+}  // namespace abft
+
+// The opaque handle of the C ABI.
+struct abft_ws {
+    int device = 0;
+    int sms = 148;
+    int M_b = 0, N_b = 0, K = 0, F = 0, nfmax = 0, nfpad = 0, max_iters = 0;
+    std::vector<int> counts, offsets;
+    void* base = nullptr;
+    size_t bytes = 0;
+    bool owns = false;
+    abft::WsDev d{};
+};
+
+namespace abft {
+
+// Error reporting (thread-local last error).
+void set_error(const std::string& msg);
+int cuda_fail(cudaError_t e, const char* what);
+
+struct WsLayout {
+    size_t colSumA, expRow, rowSumB, expCol, rec, ctr, vpart, vact, vd, vw, vcnt, lact, ld, lw, lcnt, dlog, ilog,
+        pend, total;
+};
+WsLayout ws_layout(int M_b, int N_b, int K, int F, int nfmax, int max_iters);
+
+// Kernel launchers (enqueue only). Return ABFT_OK or a negative status.
+int launch_encode(abft_ws* ws, const float* dA, int64_t lda, const float* dB, int64_t ldb, cudaStream_t st,
+                  int* launches);
+int launch_verify(abft_ws* ws, const float* dC, int64_t ldc, int f, double tau, int injected, int it,
+                  cudaStream_t st);
+int launch_localize(abft_ws* ws, float* dC, int64_t ldc, int f, double tau, int injected, const float* dG,
+                    int64_t ldg, int it, int correct_mode, cudaStream_t st);
+int launch_drain(abft_ws* ws, float* dC0, float* dC1, int64_t ldc, const float* dG, int64_t ldg, int repeats,
+                 cudaStream_t st);
+int launch_inject(float* dC, int64_t ldc, int row, int col, int mode, float delta, int bit, InjectLog* log,
+                  int frag, cudaStream_t st);
+
+}  // namespace abft

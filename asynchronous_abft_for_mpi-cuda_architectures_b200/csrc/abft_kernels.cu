@@ -1,0 +1,745 @@
+// sm_100a kernels of the asynchronous ABFT layer.
+//
+// Checksum arithmetic follows the reference's kernels
+// (kernels/abft_stepwise.cuh:9-206, kernels/swifi.cuh:33-59): FP64 sums of
+// FP32 data. The decisions (detected column, located row, corrected value)
+// are bit-identical to the reference's, whose sums run sequentially, one
+// thread per column. The fast path does not run sequentially; it is made exact
+// as follows.
+//
+// Certified fast sums. A verify CTA streams a tile of C with 128-bit loads
+// (all SMs, HBM bound) and keeps, per column, the double sum S, the float sum
+// T of |x| and the smallest nonzero |x|. Every x is an integer multiple of
+// 2^p, p = ulp exponent of the smallest nonzero |x|; when T <= 2^(p+53) every
+// partial sum of every order is a multiple of 2^p below 2^(p+53) and hence
+// exactly representable, so S equals the reference's sequential sum bit for
+// bit ("certified"). Otherwise S differs from it by at most 2*gamma_n*T and
+// the decision logic carries that window: a column whose window cannot reach
+// the threshold or the current maximum is decided without it; the few that
+// can are re-summed sequentially in the reference's order. The arg-max is then
+// the reference's own 256-slot strided scan and tree on exact values.
+//
+// Encode kernels (colSumA, expectedRow, rowSumB_f, expectedCol_f) are
+// sequential chains by definition; they run one chain per thread fed from
+// shared memory by a deep cp.async pipeline so that the chain latency, not
+// memory latency, bounds them.
+
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+#include "abft_b200.h"
+#include "abft_internal.h"
+
+namespace abft {
+namespace {
+
+constexpr unsigned kFull = 0xffffffffu;
+constexpr int kListCap = 256;
+
+// ------------------------------------------------------------- helpers ----
+
+__device__ __forceinline__ double2 pack_partial(double s, float t, uint32_t mbm1) {
+    unsigned long long hi = ((unsigned long long)mbm1 << 32) | (unsigned long long)__float_as_uint(t);
+    return make_double2(s, __longlong_as_double((long long)hi));
+}
+
+__device__ __forceinline__ void unpack_partial(double2 p, double& s, float& t, uint32_t& mbm1) {
+    s = p.x;
+    unsigned long long hi = (unsigned long long)__double_as_longlong(p.y);
+    t = __uint_as_float((uint32_t)(hi & 0xffffffffull));
+    mbm1 = (uint32_t)(hi >> 32);
+}
+
+// Window w >= 0 with |d_reference - d| <= w for a sum S of n float terms with
+// float |x|-sum T and smallest (|x| bits - 1) mbm1; w == 0 means S (and so d)
+// is exactly the reference's value.
+__device__ __forceinline__ double cert_window(double S, float T, uint32_t mbm1, int n, double d) {
+    if (!isfinite(S)) return 0.0;  // NaN/Inf data: every order gives the same class
+    const uint32_t nz = mbm1 + 1u;
+    if (nz == 0u) return 0.0;  // all terms are +-0
+    if (n > (1 << 21)) return INFINITY;
+    int e = (int)(nz >> 23);
+    if (e < 1) e = 1;
+    const double tb = (double)T * (1.0 + 4.0 * (double)n * 0x1p-24);  // upper bound of sum |x|
+    if (tb <= ldexp(1.0, e - 97)) return 0.0;                          // 2^(p+53), p = e - 150
+    const double E = 2.0 * (double)n * 0x1p-53 * tb * (1.0 + 0x1p-30);
+    const double w = E * (1.0 + 0x1p-40) + d * 0x1p-51 + 0x1p-1000;
+    return (w > 0.0) ? w : INFINITY;
+}
+
+__device__ __forceinline__ void acc1(float x, double& s, float& t, uint32_t& m) {
+    s = __dadd_rn(s, (double)x);
+    t += fabsf(x);
+    m = min(m, (__float_as_uint(x) & 0x7fffffffu) - 1u);
+}
+
+// Sequential double sum x[0] + x[stride] + ... (n terms) in ascending order,
+// starting from 0.0: the reference's per-thread loop. Warp-cooperative: lanes
+// prefetch 32 terms, every lane runs the same chain.
+__device__ double exact_chain(const float* __restrict__ x, long long stride, int n) {
+    const int lane = threadIdx.x & 31;
+    double s = 0.0;
+    float v = (lane < n) ? x[(long long)lane * stride] : 0.f;
+    for (int i0 = 0; i0 < n; i0 += 32) {
+        const int nx = i0 + 32 + lane;
+        const float vn = (nx < n) ? x[(long long)nx * stride] : 0.f;
+        if (n - i0 >= 32) {
+#pragma unroll
+            for (int r = 0; r < 32; ++r) s = __dadd_rn(s, (double)__shfl_sync(kFull, v, r));
+        } else {
+            const int m = n - i0;
+            for (int r = 0; r < 32; ++r) {
+                const float y = __shfl_sync(kFull, v, r);
+                if (r < m) s = __dadd_rn(s, (double)y);
+            }
+        }
+        v = vn;
+    }
+    return s;
+}
+
+struct SelectSmem {
+    double d[kThreads];
+    int j[kThreads];
+    int list[kListCap];
+    int cnt;
+    int flag;
+};
+
+// Arg-max of k_detect_row / k_locate_correct (kernels/abft_stepwise.cuh:85-110,
+// :174-187) over n entries, run by one 256-thread CTA. act/dd/ww hold the fast
+// sum, its |act - exp| and window; entries that could change the outcome are
+// first re-summed exactly by `exact(j)` (warp-cooperative). Returns the
+// reference's winner or -1.
+template <class Exact>
+__device__ int final_select(int n, double tau, const double* __restrict__ expv, double* act, double* dd, double* ww,
+                            Exact exact, SelectSmem& sm) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    double bc = -INFINITY;
+    for (int j = tid; j < n; j += kThreads) {
+        const double wv = __ldcg(ww + j), dv = __ldcg(dd + j);
+        if (wv == 0.0 && dv > tau && dv > bc) bc = dv;
+    }
+    sm.d[tid] = bc;
+    __syncthreads();
+    for (int s = kThreads / 2; s > 0; s >>= 1) {
+        if (tid < s && sm.d[tid + s] > sm.d[tid]) sm.d[tid] = sm.d[tid + s];
+        __syncthreads();
+    }
+    const double best_cert = sm.d[0];
+    __syncthreads();
+
+    for (;;) {
+        if (tid == 0) sm.cnt = 0;
+        __syncthreads();
+        for (int j = tid; j < n; j += kThreads) {
+            const double wv = __ldcg(ww + j);
+            if (wv != 0.0) {
+                const double hi = __ldcg(dd + j) + wv;
+                if (hi > tau && hi >= best_cert) {
+                    const int k = atomicAdd(&sm.cnt, 1);
+                    if (k < kListCap) sm.list[k] = j;
+                }
+            }
+        }
+        __syncthreads();
+        const int cnt = sm.cnt;
+        const int todo = min(cnt, kListCap);
+        for (int k = warp; k < todo; k += kWarps) {
+            const int j = sm.list[k];
+            const double S = exact(j);
+            if (lane == 0) {
+                act[j] = S;
+                dd[j] = fabs(S - expv[j]);
+                ww[j] = 0.0;
+            }
+        }
+        __syncthreads();
+        if (cnt <= kListCap) break;
+    }
+
+    double best = 0.0;
+    int bj = -1;
+    for (int j = tid; j < n; j += kThreads) {
+        if (__ldcg(ww + j) == 0.0) {
+            const double dv = __ldcg(dd + j);
+            if (dv > tau && dv > best) {
+                best = dv;
+                bj = j;
+            }
+        }
+    }
+    sm.d[tid] = best;
+    sm.j[tid] = bj;
+    __syncthreads();
+    for (int s = kThreads / 2; s > 0; s >>= 1) {
+        if (tid < s && sm.d[tid + s] > sm.d[tid]) {
+            sm.d[tid] = sm.d[tid + s];
+            sm.j[tid] = sm.j[tid + s];
+        }
+        __syncthreads();
+    }
+    const int w = sm.j[0];
+    __syncthreads();
+    return w;
+}
+
+// ------------------------------------------------------------- verify -----
+
+// Fused actualRow + detect for one fragment (M x N, leading dimension ldc).
+// grid = (groups of 128 columns, row chunks). Each CTA reduces its tile into
+// per-column partials; the last CTA of a column group folds the partials and
+// certifies each column; the last group runs the reference's arg-max.
+template <bool VEC>
+__global__ void __launch_bounds__(kThreads)
+    k_verify(const float* __restrict__ C, long long ldc, int M, int N, int rows_per, int chunks, int groups,
+             int nfpad, const double* __restrict__ expv, double tau, int injected, int f, int F, int it, WsDev w) {
+    __shared__ double s_s[kWarps][kGroupCols];
+    __shared__ float s_t[kWarps][kGroupCols];
+    __shared__ uint32_t s_m[kWarps][kGroupCols];
+    __shared__ SelectSmem sel;
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = blockIdx.x, chunk = blockIdx.y;
+    const int c0 = g * kGroupCols + lane * 4;
+    const int r0 = chunk * rows_per;
+    const int r1 = min(M, r0 + rows_per);
+
+    double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
+    float t0 = 0.f, t1 = 0.f, t2 = 0.f, t3 = 0.f;
+    uint32_t m0 = kFull, m1 = kFull, m2 = kFull, m3 = kFull;
+
+    auto load = [&](int r) -> float4 {
+        const float* p = C + (long long)r * ldc + c0;
+        if (VEC) {
+            if (c0 < N) return __ldg(reinterpret_cast<const float4*>(p));
+            return make_float4(0.f, 0.f, 0.f, 0.f);
+        } else {
+            float4 v;
+            v.x = (c0 + 0 < N) ? __ldg(p + 0) : 0.f;
+            v.y = (c0 + 1 < N) ? __ldg(p + 1) : 0.f;
+            v.z = (c0 + 2 < N) ? __ldg(p + 2) : 0.f;
+            v.w = (c0 + 3 < N) ? __ldg(p + 3) : 0.f;
+            return v;
+        }
+    };
+    auto acc = [&](float4 v) {
+        acc1(v.x, s0, t0, m0);
+        acc1(v.y, s1, t1, m1);
+        acc1(v.z, s2, t2, m2);
+        acc1(v.w, s3, t3, m3);
+    };
+
+    int r = r0 + warp;
+    for (; r + 7 * kWarps < r1; r += 8 * kWarps) {
+        float4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = load(r + u * kWarps);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) acc(v[u]);
+    }
+    for (; r < r1; r += kWarps) acc(load(r));
+
+    const int cl = lane * 4;
+    s_s[warp][cl + 0] = s0; s_s[warp][cl + 1] = s1; s_s[warp][cl + 2] = s2; s_s[warp][cl + 3] = s3;
+    s_t[warp][cl + 0] = t0; s_t[warp][cl + 1] = t1; s_t[warp][cl + 2] = t2; s_t[warp][cl + 3] = t3;
+    s_m[warp][cl + 0] = m0; s_m[warp][cl + 1] = m1; s_m[warp][cl + 2] = m2; s_m[warp][cl + 3] = m3;
+    __syncthreads();
+    if (tid < kGroupCols) {
+        const int col = g * kGroupCols + tid;
+        if (col < N) {
+            double S = 0.0;
+            float T = 0.f;
+            uint32_t mb = kFull;
+#pragma unroll
+            for (int k = 0; k < kWarps; ++k) {
+                S = __dadd_rn(S, s_s[k][tid]);
+                T += s_t[k][tid];
+                mb = min(mb, s_m[k][tid]);
+            }
+            reinterpret_cast<double2*>(w.vpart)[(long long)chunk * nfpad + col] = pack_partial(S, T, mb);
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) sel.flag = (atomicAdd(&w.vcnt[g], 1) == chunks - 1);
+    __syncthreads();
+    if (!sel.flag) return;
+    __threadfence();
+
+    // Last CTA of column group g: fold the row-chunk partials in chunk order.
+    if (tid < kGroupCols) {
+        const int col = g * kGroupCols + tid;
+        if (col < N) {
+            double S = 0.0;
+            float T = 0.f;
+            uint32_t mb = kFull;
+            const double2* pp = reinterpret_cast<const double2*>(w.vpart);
+            for (int ch = 0; ch < chunks; ++ch) {
+                double ps;
+                float pt;
+                uint32_t pm;
+                unpack_partial(__ldcg(pp + (long long)ch * nfpad + col), ps, pt, pm);
+                S = __dadd_rn(S, ps);
+                T += pt;
+                mb = min(mb, pm);
+            }
+            const double d = fabs(S - expv[col]);
+            w.vact[col] = S;
+            w.vd[col] = d;
+            w.vw[col] = cert_window(S, T, mb, M, d);
+        }
+    }
+    if (tid == 0) w.vcnt[g] = 0;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) sel.flag = (atomicAdd(&w.vcnt[groups], 1) == groups - 1);
+    __syncthreads();
+    if (!sel.flag) return;
+    __threadfence();
+
+    // Last group: the reference's detection (k_detect_row) on exact values.
+    const int ec = final_select(
+        N, tau, expv, w.vact, w.vd, w.vw, [&](int j) { return exact_chain(C + j, ldc, M); }, sel);
+    if (tid == 0) {
+        const double rd = (ec >= 0) ? (__ldcg(w.vact + ec) - expv[ec]) : 0.0;
+        w.rec[f].errcol = ec;
+        w.rec[f].errrow = -1;
+        w.rec[f].rowdiff = rd;
+        const int det = ec >= 0;
+        const int idx = injected ? (det ? 0 : 3) : (det ? 2 : 1);
+        atomicAdd(&w.ctr->cm[idx], 1);
+        if (it >= 0) {
+            DecisionLog& L = w.dlog[(long long)it * F + f];
+            L.errcol = ec;
+            L.errrow = -1;
+            L.rowdiff = rd;
+        }
+        w.vcnt[groups] = 0;
+    }
+}
+
+// ----------------------------------------------------------- localise -----
+
+// Gated localisation + correction for one fragment: row sums of the fragment
+// (warp per row), certified like the column sums, then the reference's row
+// arg-max (k_locate_correct) and the correction C = float(double(C) - rowdiff).
+template <bool VEC>
+__global__ void __launch_bounds__(kThreads)
+    k_localize(float* C, long long ldc, int M, int N, int rows_per, int nblocks, const double* __restrict__ expc,
+               double tau, int injected, const float* __restrict__ G, long long ldg, int frag_off, int f, int F,
+               int it, int drain, int pend_cap, WsDev w) {
+    __shared__ SelectSmem sel;
+    const int ec = __ldcg(&w.rec[f].errcol);
+    if (ec < 0) return;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int r0 = blockIdx.x * rows_per;
+    const int r1 = min(M, r0 + rows_per);
+    for (int r = r0 + warp; r < r1; r += kWarps) {
+        const float* row = C + (long long)r * ldc;
+        double s = 0.0;
+        float t = 0.f;
+        uint32_t m = kFull;
+        if (VEC) {
+#pragma unroll 4
+            for (int c = lane * 4; c < N; c += 128) {
+                const float4 v = __ldg(reinterpret_cast<const float4*>(row + c));
+                acc1(v.x, s, t, m);
+                acc1(v.y, s, t, m);
+                acc1(v.z, s, t, m);
+                acc1(v.w, s, t, m);
+            }
+        } else {
+#pragma unroll 4
+            for (int c = lane; c < N; c += 32) acc1(__ldg(row + c), s, t, m);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            s = __dadd_rn(s, __shfl_xor_sync(kFull, s, o));
+            t += __shfl_xor_sync(kFull, t, o);
+            m = min(m, __shfl_xor_sync(kFull, m, o));
+        }
+        if (lane == 0) {
+            const double d = fabs(s - expc[r]);
+            w.lact[r] = s;
+            w.ld[r] = d;
+            w.lw[r] = cert_window(s, t, m, N, d);
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) sel.flag = (atomicAdd(w.lcnt, 1) == nblocks - 1);
+    __syncthreads();
+    if (!sel.flag) return;
+    __threadfence();
+
+    const int er = final_select(
+        M, tau, expc, w.lact, w.ld, w.lw, [&](int i) { return exact_chain(C + (long long)i * ldc, 1, N); }, sel);
+    if (tid == 0) {
+        *w.lcnt = 0;
+        const double rd = __ldcg(&w.rec[f].rowdiff);
+        if (er >= 0) {
+            float* p = C + (long long)er * ldc + ec;
+            const float cf = __ldcg(p);
+            const float c = static_cast<float>(static_cast<double>(cf) - rd);
+            if (drain) {
+                const int k = atomicAdd(&w.ctr->n_pending, 1);
+                if (k < pend_cap) {
+                    PendingFix& q = w.pend[k];
+                    q.it = it; q.f = f; q.er = er; q.ec = ec; q.injected = injected; q.off = frag_off;
+                    q.rowdiff = rd; q.tau = tau; q.c_fault = cf; q.pad = 0.f;
+                }
+            } else {
+                *p = c;
+                if (injected && G != nullptr) {
+                    const float gv = G[(long long)er * ldg + frag_off + ec];
+                    if (fabs(static_cast<double>(c) - static_cast<double>(gv)) <= tau) atomicAdd(&w.ctr->n_restored, 1);
+                }
+            }
+        }
+        w.rec[f].errrow = er;
+        if (it >= 0) w.dlog[(long long)it * F + f].errrow = er;
+    }
+}
+
+// Post-loop drain: one thread per queued fix.
+__global__ void k_drain(float* C0, float* C1, long long ldc, const float* G, long long ldg, int repeats, int cap,
+                        WsDev w) {
+    const int n = min(__ldcg(&w.ctr->n_pending), cap);
+    for (int k = blockIdx.x * blockDim.x + threadIdx.x; k < n; k += gridDim.x * blockDim.x) {
+        const PendingFix q = w.pend[k];
+        const int off = q.off;
+        const float c = static_cast<float>(static_cast<double>(q.c_fault) - q.rowdiff);
+        if (q.it >= repeats - 2) {
+            float* C = (q.it % 2 == 0) ? C0 : C1;
+            C[(long long)q.er * ldc + off + q.ec] = c;
+        }
+        if (q.injected && G != nullptr) {
+            const float gv = G[(long long)q.er * ldg + off + q.ec];
+            if (fabs(static_cast<double>(c) - static_cast<double>(gv)) <= q.tau) atomicAdd(&w.ctr->n_restored, 1);
+        }
+    }
+}
+
+// ----------------------------------------------------------- injectors ----
+
+__global__ void k_inject(float* C, long long ldc, int row, int col, int mode, float delta, int bit, InjectLog* log,
+                         int frag) {
+    float* p = C + (long long)row * ldc + col;
+    const float before = *p;
+    const float after = (mode == ABFT_INJECT_ADD) ? __fadd_rn(before, delta)
+                                                  : __uint_as_float(__float_as_uint(before) ^ (1u << bit));
+    *p = after;
+    if (log != nullptr) {
+        log->frag = frag;
+        log->row = row;
+        log->col = col;
+        log->bit = (mode == ABFT_INJECT_ADD) ? -1 : bit;
+        log->before = before;
+        log->after = after;
+    }
+}
+
+// ------------------------------------------------------------- encode -----
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src_bytes) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(src_bytes));
+}
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem, int src_bytes) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(s), "l"(gmem), "r"(src_bytes));
+}
+__device__ __forceinline__ void cp_async8(void* smem, const void* gmem, int src_bytes) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n" ::"r"(s), "l"(gmem), "r"(src_bytes));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+
+constexpr int kColStages = 16;  // 16 x 32 rows x 32 columns x 4 B = 64 KB
+constexpr int kColSmem = kColStages * 32 * 32 * 4;
+
+// Column chains: out[c] = sequential sum over rows r of X[r, c] (WEIGHTED:
+// fused multiply-add chain with per-row weight wrow[r]). One warp = 32 columns.
+// Replaces k_col_checksum_A (abft_stepwise.cuh:9-18) and k_expected_row (:31-41).
+template <bool WEIGHTED, bool VEC>
+__global__ void __launch_bounds__(32)
+    k_colchain(const float* __restrict__ X, long long ld, int R, int ncols, const double* __restrict__ wrow,
+               double* __restrict__ out) {
+    extern __shared__ __align__(16) float tile[];
+    const int lane = threadIdx.x;
+    const int cbase = blockIdx.x * 32;
+    const int ncv = min(32, ncols - cbase);
+    const int nblk = (R + 31) / 32;
+    auto issue = [&](int blk) {
+        if (blk < nblk) {
+            float* t = tile + (blk % kColStages) * 32 * 32;
+            const int rb0 = blk * 32;
+            if (VEC) {
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const int q = lane + 32 * u;
+                    const int rr = q >> 3, cc = (q & 7) * 4;
+                    const int r = rb0 + rr;
+                    const bool ok = (r < R) && (cc < ncv);
+                    const float* src = ok ? (X + (long long)r * ld + cbase + cc) : X;
+                    cp_async16(t + rr * 32 + cc, src, ok ? 4 * min(4, ncv - cc) : 0);
+                }
+            } else {
+                for (int rr = 0; rr < 32; ++rr) {
+                    const int r = rb0 + rr;
+                    const bool ok = (r < R) && (lane < ncv);
+                    const float* src = ok ? (X + (long long)r * ld + cbase + lane) : X;
+                    cp_async4(t + rr * 32 + lane, src, ok ? 4 : 0);
+                }
+            }
+        }
+        cp_async_commit();
+    };
+    for (int b = 0; b < kColStages - 1; ++b) issue(b);
+    double s = 0.0;
+    for (int blk = 0; blk < nblk; ++blk) {
+        cp_async_wait<kColStages - 2>();
+        __syncwarp();
+        const float* t = tile + (blk % kColStages) * 32 * 32;
+        const int rb0 = blk * 32;
+        const int nr = min(32, R - rb0);
+        double wv = 0.0;
+        if (WEIGHTED) wv = (rb0 + lane < R) ? __ldg(wrow + rb0 + lane) : 0.0;
+        if (nr == 32) {
+#pragma unroll
+            for (int rr = 0; rr < 32; ++rr) {
+                const double x = (double)t[rr * 32 + lane];
+                if (WEIGHTED) s = __fma_rn(__shfl_sync(kFull, wv, rr), x, s);
+                else s = __dadd_rn(s, x);
+            }
+        } else {
+            for (int rr = 0; rr < 32; ++rr) {
+                const double x = (double)t[rr * 32 + lane];
+                const double wr = WEIGHTED ? __shfl_sync(kFull, wv, rr) : 0.0;
+                if (rr < nr) s = WEIGHTED ? __fma_rn(wr, x, s) : __dadd_rn(s, x);
+            }
+        }
+        __syncwarp();
+        issue(blk + kColStages - 1);
+    }
+    cp_async_wait<0>();
+    if (lane < ncv) out[cbase + lane] = s;
+}
+
+constexpr int kRowStages = 8;
+constexpr int kRowAcc = 4;
+
+// Row chains: for a in [0, nacc): out[a*ostride + r] = sequential sum over
+// columns c of X[r, c] (weighted: fused multiply-add with W[a*wstride + c]).
+// One warp = 32 rows; tiles of 32 x 32 staged through padded shared memory.
+// Replaces k_row_checksum_B_g (abft_stepwise.cuh:121-132) and
+// k_expected_col_g (:134-146).
+template <bool WEIGHTED>
+__global__ void __launch_bounds__(32)
+    k_rowchain(const float* __restrict__ X, long long ld, int R, int L, const double* __restrict__ W,
+               long long wstride, int nacc, double* __restrict__ out, long long ostride) {
+    __shared__ float tile[kRowStages][32][33];
+    __shared__ __align__(16) double wsm[kRowStages][kRowAcc][32];
+    const int lane = threadIdx.x;
+    const int rbase = blockIdx.x * 32;
+    const int nrv = min(32, R - rbase);
+    const int nblk = (L + 31) / 32;
+    const double* Wg = WEIGHTED ? W + (long long)blockIdx.y * kRowAcc * wstride : nullptr;
+    const int na = WEIGHTED ? min(kRowAcc, nacc - (int)blockIdx.y * kRowAcc) : 1;
+    auto issue = [&](int blk) {
+        if (blk < nblk) {
+            const int slot = blk % kRowStages;
+            const int c = blk * 32 + lane;
+            for (int rr = 0; rr < 32; ++rr) {
+                const bool ok = (rr < nrv) && (c < L);
+                const float* src = ok ? (X + (long long)(rbase + rr) * ld + c) : X;
+                cp_async4(&tile[slot][rr][lane], src, ok ? 4 : 0);
+            }
+            if (WEIGHTED) {
+                for (int a = 0; a < kRowAcc; ++a) {
+                    const bool ok = (a < na) && (c < L);
+                    const double* src = ok ? (Wg + (long long)a * wstride + c) : W;
+                    cp_async8(&wsm[slot][a][lane], src, ok ? 8 : 0);
+                }
+            }
+        }
+        cp_async_commit();
+    };
+    for (int b = 0; b < kRowStages - 1; ++b) issue(b);
+    double s[kRowAcc] = {0.0, 0.0, 0.0, 0.0};
+    for (int blk = 0; blk < nblk; ++blk) {
+        cp_async_wait<kRowStages - 2>();
+        __syncwarp();
+        const int slot = blk % kRowStages;
+        const int nc = min(32, L - blk * 32);
+        if (nc == 32) {
+#pragma unroll 8
+            for (int c = 0; c < 32; ++c) {
+                const double x = (double)tile[slot][lane][c];
+                if (WEIGHTED) {
+#pragma unroll
+                    for (int a = 0; a < kRowAcc; ++a) s[a] = __fma_rn(x, wsm[slot][a][c], s[a]);
+                } else {
+                    s[0] = __dadd_rn(s[0], x);
+                }
+            }
+        } else {
+            for (int c = 0; c < nc; ++c) {
+                const double x = (double)tile[slot][lane][c];
+                if (WEIGHTED) {
+#pragma unroll
+                    for (int a = 0; a < kRowAcc; ++a) s[a] = __fma_rn(x, wsm[slot][a][c], s[a]);
+                } else {
+                    s[0] = __dadd_rn(s[0], x);
+                }
+            }
+        }
+        __syncwarp();
+        issue(blk + kRowStages - 1);
+    }
+    cp_async_wait<0>();
+    if (lane < nrv) {
+        for (int a = 0; a < na; ++a) out[((long long)blockIdx.y * kRowAcc + a) * ostride + rbase + lane] = s[a];
+    }
+}
+
+bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+int check_launch(const char* what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, what);
+    return ABFT_OK;
+}
+
+// Verify geometry: column groups x row chunks, about two CTAs per SM.
+void verify_geometry(int sms, int M, int N, int& groups, int& chunks, int& rows_per) {
+    groups = (N + kGroupCols - 1) / kGroupCols;
+    int target = 2 * sms;
+    chunks = (target + groups - 1) / groups;
+    if (chunks < 1) chunks = 1;
+    if (chunks > kMaxChunks) chunks = kMaxChunks;
+    rows_per = (M + chunks - 1) / chunks;
+    rows_per = ((rows_per + kWarps - 1) / kWarps) * kWarps;
+    chunks = (M + rows_per - 1) / rows_per;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------ launchers ---
+
+int launch_encode(abft_ws* ws, const float* dA, int64_t lda, const float* dB, int64_t ldb, cudaStream_t st,
+                  int* launches) {
+    static bool attr_done = false;
+    if (!attr_done) {
+        cudaFuncSetAttribute(k_colchain<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kColSmem);
+        cudaFuncSetAttribute(k_colchain<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kColSmem);
+        cudaFuncSetAttribute(k_colchain<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kColSmem);
+        cudaFuncSetAttribute(k_colchain<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kColSmem);
+        attr_done = true;
+    }
+    const int M = ws->M_b, K = ws->K, N = ws->N_b, F = ws->F;
+    int n = 0;
+    // colSumA[K]: chains over the M rows of A.
+    {
+        const bool vec = aligned16(dA) && (lda % 4 == 0);
+        dim3 grid((K + 31) / 32);
+        if (vec) k_colchain<false, true><<<grid, 32, kColSmem, st>>>(dA, lda, M, K, nullptr, ws->d.colSumA);
+        else k_colchain<false, false><<<grid, 32, kColSmem, st>>>(dA, lda, M, K, nullptr, ws->d.colSumA);
+        ++n;
+        if (int rc = check_launch("encode colSumA")) return rc;
+    }
+    // expRow[N_b]: fused multiply-add chains over the K rows of B.
+    {
+        const bool vec = aligned16(dB) && (ldb % 4 == 0);
+        dim3 grid((N + 31) / 32);
+        if (vec) k_colchain<true, true><<<grid, 32, kColSmem, st>>>(dB, ldb, K, N, ws->d.colSumA, ws->d.expRow);
+        else k_colchain<true, false><<<grid, 32, kColSmem, st>>>(dB, ldb, K, N, ws->d.colSumA, ws->d.expRow);
+        ++n;
+        if (int rc = check_launch("encode expectedRow")) return rc;
+    }
+    // rowSumB_f[K] per fragment: chains over the fragment's columns of each B row.
+    for (int f = 0; f < F; ++f) {
+        dim3 grid((K + 31) / 32, 1);
+        k_rowchain<false><<<grid, 32, 0, st>>>(dB + ws->offsets[f], ldb, K, ws->counts[f], nullptr, 0, 1,
+                                               ws->d.rowSumB + (long long)f * K, 0);
+        ++n;
+        if (int rc = check_launch("encode rowSumB")) return rc;
+    }
+    // expCol_f[M_b]: fused multiply-add chains over each A row, four fragments per pass.
+    {
+        dim3 grid((M + 31) / 32, (F + kRowAcc - 1) / kRowAcc);
+        k_rowchain<true><<<grid, 32, 0, st>>>(dA, lda, M, K, ws->d.rowSumB, K, F, ws->d.expCol, M);
+        ++n;
+        if (int rc = check_launch("encode expectedCol")) return rc;
+    }
+    if (launches) *launches += n;
+    return ABFT_OK;
+}
+
+int launch_verify(abft_ws* ws, const float* dC, int64_t ldc, int f, double tau, int injected, int it,
+                  cudaStream_t st) {
+    const int M = ws->M_b, N = ws->counts[f];
+    const float* Cf = dC + ws->offsets[f];
+    int groups, chunks, rows_per;
+    verify_geometry(ws->sms, M, N, groups, chunks, rows_per);
+    const bool vec = aligned16(Cf) && (ldc % 4 == 0) && (N % 4 == 0);
+    dim3 grid(groups, chunks);
+    const double* expv = ws->d.expRow + ws->offsets[f];
+    if (it >= ws->max_iters) it = -1;
+    if (vec)
+        k_verify<true><<<grid, kThreads, 0, st>>>(Cf, ldc, M, N, rows_per, chunks, groups, ws->nfpad, expv, tau,
+                                                  injected, f, ws->F, it, ws->d);
+    else
+        k_verify<false><<<grid, kThreads, 0, st>>>(Cf, ldc, M, N, rows_per, chunks, groups, ws->nfpad, expv, tau,
+                                                   injected, f, ws->F, it, ws->d);
+    return check_launch("verify");
+}
+
+int launch_localize(abft_ws* ws, float* dC, int64_t ldc, int f, double tau, int injected, const float* dG,
+                    int64_t ldg, int it, int correct_mode, cudaStream_t st) {
+    const int M = ws->M_b, N = ws->counts[f];
+    float* Cf = dC + ws->offsets[f];
+    // about 64 KB of C per CTA, whole warps of rows
+    long long rows = 65536 / ((long long)N * 4);
+    if (rows < kWarps) rows = kWarps;
+    if (rows > 256) rows = 256;
+    int rows_per = (int)((rows + kWarps - 1) / kWarps) * kWarps;
+    int nblocks = (M + rows_per - 1) / rows_per;
+    const bool vec = aligned16(Cf) && (ldc % 4 == 0) && (N % 4 == 0);
+    const double* expc = ws->d.expCol + (long long)f * M;
+    if (it >= ws->max_iters) it = -1;
+    const int drain = (correct_mode == ABFT_CORRECT_DRAIN) ? 1 : 0;
+    const int cap = ws->max_iters * ws->F;
+    if (drain && (cap <= 0 || it < 0)) {
+        set_error("drain correction needs a workspace with max_iters > iteration index");
+        return ABFT_ERR_ARG;
+    }
+    if (vec)
+        k_localize<true><<<nblocks, kThreads, 0, st>>>(Cf, ldc, M, N, rows_per, nblocks, expc, tau, injected, dG,
+                                                       ldg, ws->offsets[f], f, ws->F, it, drain, cap, ws->d);
+    else
+        k_localize<false><<<nblocks, kThreads, 0, st>>>(Cf, ldc, M, N, rows_per, nblocks, expc, tau, injected, dG,
+                                                        ldg, ws->offsets[f], f, ws->F, it, drain, cap, ws->d);
+    return check_launch("localize");
+}
+
+int launch_drain(abft_ws* ws, float* dC0, float* dC1, int64_t ldc, const float* dG, int64_t ldg, int repeats,
+                 cudaStream_t st) {
+    const int cap = ws->max_iters * ws->F;
+    k_drain<<<1, kThreads, 0, st>>>(dC0, dC1, ldc, dG, ldg, repeats, cap, ws->d);
+    return check_launch("drain");
+}
+
+int launch_inject(float* dC, int64_t ldc, int row, int col, int mode, float delta, int bit, InjectLog* log,
+                  int frag, cudaStream_t st) {
+    k_inject<<<1, 1, 0, st>>>(dC, ldc, row, col, mode, delta, bit, log, frag);
+    return check_launch("inject");
+}
+
+}  // namespace abft

@@ -1,0 +1,468 @@
+// One rank's online ABFT pipeline: the host scheduler of pass_baseline and
+// pass_online_loop (pipeline/passes.cuh:14-35, :90-227) on B200.
+//
+// Streams: the protected SGEMMs run on a high-priority compute stream, every
+// ABFT kernel on a low-priority verify stream, so verification fills the SMs
+// the SGEMM leaves idle (wave tails, gaps between fragments) instead of
+// competing with it. Per iteration it:
+//   compute: [wait slot's verify_done] SGEMM f -> (inject) -> record compute_done[f]   (f = 0..F-1)
+//   verify : wait compute_done[f] -> fused verify f -> gated localise/correct f         (f = 0..F-1)
+//            -> record slot's verify_done
+// The two dC buffers are the two OnlineSlots: iteration k+2 reuses slot k%2
+// only after iteration k's verification finished, so iteration k's checks
+// overlap iteration k+1's SGEMMs. Injection positions come from the host RNG
+// (the reference's draws) and are passed as kernel arguments: no host
+// synchronisation inside the loop.
+
+#include <cublas_v2.h>
+#include <cuda_runtime.h>
+
+#include <chrono>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "abft_b200.h"
+#include "abft_internal.h"
+
+using namespace abft;
+
+struct abft_session {
+    int device = 0;
+    int M_b = 0, N_b = 0, K = 0, F = 0;
+    std::vector<int> counts, offsets;
+    const float* dA = nullptr;
+    int64_t lda = 0;
+    const float* dB = nullptr;
+    int64_t ldb = 0;
+    float* dC[2] = {nullptr, nullptr};
+    int64_t ldc = 0;
+    cudaStream_t compute = nullptr, verify = nullptr;
+    cublasHandle_t handle = nullptr;
+    std::vector<cudaEvent_t> compute_done;
+    cudaEvent_t buf_done[2] = {nullptr, nullptr};
+    cudaEvent_t t0 = nullptr, t1 = nullptr, vjoin = nullptr, cjoin = nullptr;
+    std::vector<cudaEvent_t> vprof;
+    abft_ws* ws = nullptr;
+    std::vector<double> tau;
+    const float* dG = nullptr;
+    int64_t ldg = 0;
+    bool encoded = false;
+    int profile = 0;
+    int max_iters = 0;
+    int last_launches = 0;
+};
+
+namespace {
+
+#define CK(call)                                                     \
+    do {                                                             \
+        cudaError_t e_ = (call);                                     \
+        if (e_ != cudaSuccess) return cuda_fail(e_, #call);          \
+    } while (0)
+
+#define RC(call)                                                     \
+    do {                                                             \
+        int rc_ = (call);                                            \
+        if (rc_ != ABFT_OK) return rc_;                              \
+    } while (0)
+
+int sgemm_frag(abft_session* s, float* dC, int f) {
+    const int off = s->offsets[f];
+    return abft_sgemm(s->handle, s->dA, (int)s->lda, s->dB + off, (int)s->ldb, dC + off, (int)s->ldc, s->M_b,
+                      s->counts[f], s->K);
+}
+
+// gemm_warmup, kernels/gemm_cublas.cuh:25-42: three 64^3 SGEMMs so that
+// library loading and heuristics happen before any timed region.
+int gemm_warmup(abft_session* s) {
+    constexpr int W = 64;
+    float* buf = nullptr;
+    CK(cudaMalloc(&buf, sizeof(float) * W * W * 3));
+    CK(cudaMemsetAsync(buf, 0, sizeof(float) * W * W * 3, s->compute));
+    for (int i = 0; i < 3; ++i) {
+        int rc = abft_sgemm(s->handle, buf, W, buf + W * W, W, buf + 2 * W * W, W, W, W, W);
+        if (rc != ABFT_OK) {
+            cudaFree(buf);
+            return rc;
+        }
+    }
+    CK(cudaStreamSynchronize(s->compute));
+    CK(cudaFree(buf));
+    return ABFT_OK;
+}
+
+struct Plan {
+    int frag, row, col, bit;
+};
+
+// Enqueue `repeats` protected iterations on the two streams (no host sync).
+int enqueue_loop(abft_session* s, const abft_online_args* a, const std::vector<Plan>& plan, int* launches,
+                 int* vlaunches) {
+    const bool inject_on = (a->mode == ABFT_INJECT_ADD || a->mode == ABFT_INJECT_SWIFI);
+    const bool do_localize = inject_on;
+    bool used[2] = {false, false};
+    int nl = 0, nv = 0;
+    for (int it = 0; it < a->repeats; ++it) {
+        const int bi = it & 1;
+        float* dC = s->dC[bi];
+        if (used[bi]) CK(cudaStreamWaitEvent(s->compute, s->buf_done[bi], 0));
+        const int log_it = (a->log && it < s->max_iters) ? it : -1;
+        for (int f = 0; f < s->F; ++f) {
+            RC(sgemm_frag(s, dC, f));
+            if (f == plan[it].frag) {
+                InjectLog* lg = (log_it >= 0) ? s->ws->d.ilog + log_it : nullptr;
+                const int mode = (a->mode == ABFT_INJECT_ADD) ? ABFT_INJECT_ADD : ABFT_INJECT_SWIFI;
+                RC(launch_inject(dC + s->offsets[f], s->ldc, plan[it].row, plan[it].col, mode, a->add_delta,
+                                 plan[it].bit, lg, f, s->compute));
+                ++nl;
+            }
+            CK(cudaEventRecord(s->compute_done[f], s->compute));
+        }
+        for (int f = 0; f < s->F; ++f) {
+            const int injected = (f == plan[it].frag) ? 1 : 0;
+            CK(cudaStreamWaitEvent(s->verify, s->compute_done[f], 0));
+            const bool prof = s->profile && (size_t)(2 * nv + 1) < s->vprof.size();
+            if (prof) CK(cudaEventRecord(s->vprof[2 * nv], s->verify));
+            RC(launch_verify(s->ws, dC, s->ldc, f, s->tau[f], injected, log_it, s->verify));
+            if (prof) CK(cudaEventRecord(s->vprof[2 * nv + 1], s->verify));
+            ++nl;
+            ++nv;
+            if (do_localize) {
+                RC(launch_localize(s->ws, dC, s->ldc, f, s->tau[f], injected, s->dG, s->ldg, it, a->correct_mode,
+                                   s->verify));
+                ++nl;
+            }
+        }
+        CK(cudaEventRecord(s->buf_done[bi], s->verify));
+        used[bi] = true;
+    }
+    if (do_localize && a->correct_mode == ABFT_CORRECT_DRAIN) {
+        RC(launch_drain(s->ws, s->dC[0], s->dC[1], s->ldc, s->dG, s->ldg, a->repeats, s->verify));
+        ++nl;
+    }
+    *launches = nl;
+    *vlaunches = nv;
+    return ABFT_OK;
+}
+
+int make_plan(abft_session* s, const abft_online_args* a, std::vector<Plan>& plan) {
+    plan.assign(a->repeats, Plan{-1, -1, -1, -1});
+    for (int it = 0; it < a->repeats; ++it) {
+        RC(abft_injection_plan(a->base_seed, a->rank, it, s->F, s->M_b, s->counts.data(), a->mode, a->zone_lo,
+                               a->zone_hi, &plan[it].frag, &plan[it].row, &plan[it].col, &plan[it].bit));
+    }
+    return ABFT_OK;
+}
+
+int check_args(abft_session* s, const abft_online_args* a) {
+    if (!a || a->repeats < 0 || (a->mode < ABFT_INJECT_NONE || a->mode > ABFT_INJECT_SWIFI) ||
+        (a->correct_mode != ABFT_CORRECT_INLOOP && a->correct_mode != ABFT_CORRECT_DRAIN)) {
+        set_error("online: bad arguments");
+        return ABFT_ERR_ARG;
+    }
+    if ((int)s->tau.size() != s->F) {
+        set_error("online: thresholds not set (abft_session_set_tau)");
+        return ABFT_ERR_STATE;
+    }
+    if (a->correct_mode == ABFT_CORRECT_DRAIN && a->mode != ABFT_INJECT_NONE && a->repeats > s->max_iters) {
+        set_error("online: drain correction needs repeats <= max_iters");
+        return ABFT_ERR_ARG;
+    }
+    return ABFT_OK;
+}
+
+int ensure_prof_events(abft_session* s, int n_verify) {
+    if (!s->profile) return ABFT_OK;
+    while ((int)s->vprof.size() < 2 * n_verify) {
+        cudaEvent_t e;
+        CK(cudaEventCreate(&e));
+        s->vprof.push_back(e);
+    }
+    return ABFT_OK;
+}
+
+void prof_stats(abft_session* s, int nv, abft_online_result* r) {
+    r->verify_ms_sum = 0.0;
+    r->verify_ms_max = 0.0;
+    if (!s->profile) return;
+    for (int k = 0; k < nv && 2 * k + 1 < (int)s->vprof.size(); ++k) {
+        float ms = 0.f;
+        if (cudaEventElapsedTime(&ms, s->vprof[2 * k], s->vprof[2 * k + 1]) == cudaSuccess) {
+            r->verify_ms_sum += ms;
+            if (ms > r->verify_ms_max) r->verify_ms_max = ms;
+        }
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+int abft_session_create(const abft_session_cfg* c, abft_session** out) {
+    if (!out || !c) {
+        set_error("abft_session_create: NULL argument");
+        return ABFT_ERR_ARG;
+    }
+    *out = nullptr;
+    if (c->M_b < 1 || c->N_b < 1 || c->K < 1 || c->F < 1 || !c->counts || !c->offsets || !c->dA || !c->dB ||
+        !c->dC0 || !c->dC1 || c->lda < c->K || c->ldb < c->N_b || c->ldc < c->N_b || c->max_iters < 0 ||
+        c->lda > 0x7fffffff || c->ldb > 0x7fffffff || c->ldc > 0x7fffffff) {
+        set_error("abft_session_create: bad configuration");
+        return ABFT_ERR_ARG;
+    }
+    abft_session* s = new (std::nothrow) abft_session();
+    if (!s) {
+        set_error("out of host memory");
+        return ABFT_ERR_ARG;
+    }
+    s->M_b = c->M_b;
+    s->N_b = c->N_b;
+    s->K = c->K;
+    s->F = c->F;
+    s->counts.assign(c->counts, c->counts + c->F);
+    s->offsets.assign(c->offsets, c->offsets + c->F);
+    s->dA = c->dA;
+    s->lda = c->lda;
+    s->dB = c->dB;
+    s->ldb = c->ldb;
+    s->dC[0] = c->dC0;
+    s->dC[1] = c->dC1;
+    s->ldc = c->ldc;
+    s->max_iters = c->max_iters;
+    auto fail = [&](int rc) {
+        abft_session_destroy(s);
+        return rc;
+    };
+    cudaError_t e = cudaGetDevice(&s->device);
+    if (e != cudaSuccess) return fail(cuda_fail(e, "cudaGetDevice"));
+    int least = 0, greatest = 0;
+    e = cudaDeviceGetStreamPriorityRange(&least, &greatest);
+    if (e != cudaSuccess) return fail(cuda_fail(e, "stream priority range"));
+    const int vprio = (c->verify_priority < 0) ? least : (c->verify_priority > 0 ? greatest : 0);
+    e = cudaStreamCreateWithPriority(&s->compute, cudaStreamNonBlocking, greatest);
+    if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&s->verify, cudaStreamNonBlocking, vprio);
+    if (e != cudaSuccess) return fail(cuda_fail(e, "stream create"));
+    if (cublasCreate(&s->handle) != CUBLAS_STATUS_SUCCESS ||
+        cublasSetStream(s->handle, s->compute) != CUBLAS_STATUS_SUCCESS) {
+        set_error("cublasCreate/cublasSetStream failed");
+        return fail(ABFT_ERR_CUBLAS);
+    }
+    s->compute_done.assign(s->F, nullptr);
+    for (int f = 0; f < s->F && e == cudaSuccess; ++f)
+        e = cudaEventCreateWithFlags(&s->compute_done[f], cudaEventDisableTiming);
+    for (int i = 0; i < 2 && e == cudaSuccess; ++i) e = cudaEventCreateWithFlags(&s->buf_done[i], cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreate(&s->t0);
+    if (e == cudaSuccess) e = cudaEventCreate(&s->t1);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s->vjoin, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s->cjoin, cudaEventDisableTiming);
+    if (e != cudaSuccess) return fail(cuda_fail(e, "event create"));
+    int rc = abft_ws_create(s->M_b, s->N_b, s->K, s->F, c->counts, c->offsets, c->max_iters, nullptr, 0, &s->ws);
+    if (rc != ABFT_OK) return fail(rc);
+    rc = gemm_warmup(s);
+    if (rc != ABFT_OK) return fail(rc);
+    *out = s;
+    return ABFT_OK;
+}
+
+int abft_session_destroy(abft_session* s) {
+    if (!s) return ABFT_OK;
+    if (s->compute) cudaStreamSynchronize(s->compute);
+    if (s->verify) cudaStreamSynchronize(s->verify);
+    for (auto e : s->compute_done)
+        if (e) cudaEventDestroy(e);
+    for (auto e : s->vprof)
+        if (e) cudaEventDestroy(e);
+    for (auto e : {s->buf_done[0], s->buf_done[1], s->t0, s->t1, s->vjoin, s->cjoin})
+        if (e) cudaEventDestroy(e);
+    if (s->handle) cublasDestroy(s->handle);
+    if (s->compute) cudaStreamDestroy(s->compute);
+    if (s->verify) cudaStreamDestroy(s->verify);
+    abft_ws_destroy(s->ws);
+    delete s;
+    return ABFT_OK;
+}
+
+abft_ws* abft_session_ws(abft_session* s) { return s ? s->ws : nullptr; }
+
+int abft_session_set_tau(abft_session* s, const double* tau) {
+    if (!s || !tau) {
+        set_error("abft_session_set_tau: NULL argument");
+        return ABFT_ERR_ARG;
+    }
+    s->tau.assign(tau, tau + s->F);
+    return ABFT_OK;
+}
+
+int abft_session_set_golden(abft_session* s, const float* dG, int64_t ldg) {
+    if (!s || (dG && ldg < s->N_b)) {
+        set_error("abft_session_set_golden: bad argument");
+        return ABFT_ERR_ARG;
+    }
+    s->dG = dG;
+    s->ldg = dG ? ldg : 0;
+    return ABFT_OK;
+}
+
+int abft_session_encode(abft_session* s, double* encode_ms) {
+    if (!s) {
+        set_error("abft_session_encode: NULL session");
+        return ABFT_ERR_ARG;
+    }
+    CK(cudaEventRecord(s->t0, s->verify));
+    RC(launch_encode(s->ws, s->dA, s->lda, s->dB, s->ldb, s->verify, nullptr));
+    CK(cudaEventRecord(s->t1, s->verify));
+    CK(cudaStreamSynchronize(s->verify));
+    float ms = 0.f;
+    CK(cudaEventElapsedTime(&ms, s->t0, s->t1));
+    if (encode_ms) *encode_ms = ms;
+    s->encoded = true;
+    return ABFT_OK;
+}
+
+int abft_session_baseline(abft_session* s, int repeats, double* device_ms, double* host_ms) {
+    if (!s || repeats < 0) {
+        set_error("abft_session_baseline: bad argument");
+        return ABFT_ERR_ARG;
+    }
+    CK(cudaStreamSynchronize(s->compute));
+    const auto h0 = std::chrono::high_resolution_clock::now();
+    CK(cudaEventRecord(s->t0, s->compute));
+    for (int it = 0; it < repeats; ++it)
+        for (int f = 0; f < s->F; ++f) RC(sgemm_frag(s, s->dC[0], f));
+    CK(cudaEventRecord(s->t1, s->compute));
+    CK(cudaEventSynchronize(s->t1));
+    const auto h1 = std::chrono::high_resolution_clock::now();
+    float ms = 0.f;
+    CK(cudaEventElapsedTime(&ms, s->t0, s->t1));
+    if (device_ms) *device_ms = ms;
+    if (host_ms) *host_ms = std::chrono::duration<double, std::milli>(h1 - h0).count();
+    return ABFT_OK;
+}
+
+int abft_session_online(abft_session* s, const abft_online_args* a, abft_online_result* r) {
+    if (!s || !r) {
+        set_error("abft_session_online: NULL argument");
+        return ABFT_ERR_ARG;
+    }
+    RC(check_args(s, a));
+    s->profile = a->profile ? 1 : 0;
+    if (!s->encoded) {
+        double ms;
+        RC(abft_session_encode(s, &ms));
+    }
+    std::vector<Plan> plan;
+    RC(make_plan(s, a, plan));
+    RC(ensure_prof_events(s, a->repeats * s->F));
+    RC(abft_ws_reset_counters(s->ws, s->verify));
+    CK(cudaStreamSynchronize(s->verify));
+    CK(cudaStreamSynchronize(s->compute));
+
+    const auto h0 = std::chrono::high_resolution_clock::now();
+    CK(cudaEventRecord(s->t0, s->compute));
+    CK(cudaStreamWaitEvent(s->verify, s->t0, 0));
+    int nl = 0, nv = 0;
+    RC(enqueue_loop(s, a, plan, &nl, &nv));
+    CK(cudaEventRecord(s->vjoin, s->verify));
+    CK(cudaStreamWaitEvent(s->compute, s->vjoin, 0));
+    CK(cudaEventRecord(s->t1, s->compute));
+    CK(cudaEventSynchronize(s->t1));
+    const auto h1 = std::chrono::high_resolution_clock::now();
+    CK(cudaGetLastError());
+
+    float ms = 0.f;
+    CK(cudaEventElapsedTime(&ms, s->t0, s->t1));
+    r->device_ms = ms;
+    r->host_ms = std::chrono::duration<double, std::milli>(h1 - h0).count();
+    RC(abft_ws_read_counters(s->ws, r->cm, &r->n_restored));
+    r->kernel_launches = nl;
+    r->verify_launches = nv;
+    prof_stats(s, nv, r);
+    s->last_launches = nl;
+    return ABFT_OK;
+}
+
+int abft_session_read_injections(abft_session* s, int it_count, int* inj4, float* before_after) {
+    if (!s || it_count < 0 || it_count > s->max_iters) {
+        set_error("abft_session_read_injections: range outside max_iters");
+        return ABFT_ERR_ARG;
+    }
+    if (it_count == 0) return ABFT_OK;
+    std::vector<InjectLog> h(it_count);
+    CK(cudaMemcpy(h.data(), s->ws->d.ilog, sizeof(InjectLog) * it_count, cudaMemcpyDeviceToHost));
+    for (int i = 0; i < it_count; ++i) {
+        if (inj4) {
+            inj4[4 * i + 0] = h[i].frag;
+            inj4[4 * i + 1] = h[i].row;
+            inj4[4 * i + 2] = h[i].col;
+            inj4[4 * i + 3] = h[i].bit;
+        }
+        if (before_after) {
+            before_after[2 * i] = h[i].before;
+            before_after[2 * i + 1] = h[i].after;
+        }
+    }
+    return ABFT_OK;
+}
+
+int abft_session_run_host(abft_session* s, const float* hA, const float* hB, float* hC, const abft_online_args* a,
+                          abft_online_result* r, double* e2e_ms) {
+    if (!s || !hA || !hB || !hC || !r) {
+        set_error("abft_session_run_host: NULL argument");
+        return ABFT_ERR_ARG;
+    }
+    RC(check_args(s, a));
+    s->profile = a->profile ? 1 : 0;
+    if (a->repeats < 1) {
+        set_error("abft_session_run_host: repeats must be >= 1");
+        return ABFT_ERR_ARG;
+    }
+    std::vector<Plan> plan;
+    RC(make_plan(s, a, plan));
+    RC(ensure_prof_events(s, a->repeats * s->F));
+    CK(cudaStreamSynchronize(s->verify));
+    CK(cudaStreamSynchronize(s->compute));
+    const auto h0 = std::chrono::high_resolution_clock::now();
+    CK(cudaEventRecord(s->t0, s->compute));
+    // inputs: host -> device (row-major stripes, possibly padded)
+    CK(cudaMemcpy2DAsync(const_cast<float*>(s->dA), sizeof(float) * s->lda, hA, sizeof(float) * s->K,
+                         sizeof(float) * s->K, s->M_b, cudaMemcpyHostToDevice, s->compute));
+    CK(cudaMemcpy2DAsync(const_cast<float*>(s->dB), sizeof(float) * s->ldb, hB, sizeof(float) * s->N_b,
+                         sizeof(float) * s->N_b, s->K, cudaMemcpyHostToDevice, s->compute));
+    CK(cudaEventRecord(s->cjoin, s->compute));
+    CK(cudaStreamWaitEvent(s->verify, s->cjoin, 0));
+    int nl = 0, nv = 0;
+    RC(abft_ws_reset_counters(s->ws, s->verify));
+    RC(launch_encode(s->ws, s->dA, s->lda, s->dB, s->ldb, s->verify, &nl));
+    s->encoded = true;
+    CK(cudaEventRecord(s->vjoin, s->verify));
+    CK(cudaStreamWaitEvent(s->compute, s->vjoin, 0));
+    int nl2 = 0;
+    RC(enqueue_loop(s, a, plan, &nl2, &nv));
+    CK(cudaEventRecord(s->vjoin, s->verify));
+    CK(cudaStreamWaitEvent(s->compute, s->vjoin, 0));
+    // result: device -> host (final buffer of the loop, and the counters)
+    const float* last = s->dC[(a->repeats - 1) & 1];
+    CK(cudaMemcpy2DAsync(hC, sizeof(float) * s->N_b, last, sizeof(float) * s->ldc, sizeof(float) * s->N_b, s->M_b,
+                         cudaMemcpyDeviceToHost, s->compute));
+    Counters hc{};
+    CK(cudaMemcpyAsync(&hc, s->ws->d.ctr, sizeof(hc), cudaMemcpyDeviceToHost, s->compute));
+    CK(cudaEventRecord(s->t1, s->compute));
+    CK(cudaEventSynchronize(s->t1));
+    const auto h1 = std::chrono::high_resolution_clock::now();
+    CK(cudaGetLastError());
+    float ms = 0.f;
+    CK(cudaEventElapsedTime(&ms, s->t0, s->t1));
+    if (e2e_ms) *e2e_ms = ms;
+    r->device_ms = ms;
+    r->host_ms = std::chrono::duration<double, std::milli>(h1 - h0).count();
+    for (int i = 0; i < 4; ++i) r->cm[i] = hc.cm[i];
+    r->n_restored = hc.n_restored;
+    r->kernel_launches = nl + nl2;
+    r->verify_launches = nv;
+    prof_stats(s, nv, r);
+    s->last_launches = nl + nl2;
+    return ABFT_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,375 @@
+#!/usr/bin/env python
+"""Protected SGEMM throughput and ABFT overhead vs unprotected cuBLAS SGEMM.
+
+Workload (per rank, weak scaling): a 4096 x 4096 C tile with K = 4096 on a
+Pr x Pc grid (global M = Pr*4096, N = Pc*4096), FP32 A and B i.i.d.
+uniform[-1,1] (mt19937_64, seeds 123456 / 987654), F = 4 column fragments,
+double-buffered C, one SWIFI single-bit flip (bit uniform over 0-31) per
+iteration, detection threshold 1e-5*K*max|A|*max|B|. One step = one trial of
+20 protected iterations (the reference's --repeats sample). A and B panels are
+broadcast from rank 0 over NCCL before timing.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Rank 0 prints one JSON line. `value` is whole-job protected TFLOP/s
+(2*M*N*K*iterations / max-over-ranks device time). `--impl reference` times
+the reference's algorithm on the host cores (CPU oracle + BLAS SGEMM).
+"""
+import argparse
+import importlib
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+PKG = "asynchronous_abft_for_mpi-cuda_architectures_b200"
+METRIC = "protected SGEMM TFLOPS and ABFT overhead % vs unprotected"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--tile", type=int, default=4096, help="per-rank C tile edge (M_b = N_b)")
+    p.add_argument("--K", type=int, default=4096)
+    p.add_argument("--frags", type=int, default=4)
+    p.add_argument("--iters", type=int, default=20, help="protected iterations per step")
+    p.add_argument("--mode", choices=["none", "add", "swifi"], default="swifi")
+    p.add_argument("--zone", default="any")
+    p.add_argument("--seed-a", type=int, default=123456)
+    p.add_argument("--seed-b", type=int, default=987654)
+    p.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU-baseline work")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-cpu", action="store_true")
+    return p.parse_args()
+
+
+def workload(args, Pr, Pc):
+    return {
+        "workload": f"protected SGEMM {args.tile}x{args.tile}x{args.K} per rank on a {Pr}x{Pc} grid "
+                    f"(global {Pr * args.tile}x{Pc * args.tile}x{args.K}), F={args.frags}, double-buffered C, "
+                    f"{args.mode} faults (zone {args.zone}), tau=1e-5*K*max|A|*max|B|",
+        "M": Pr * args.tile, "N": Pc * args.tile, "K": args.K, "tile": [args.tile, args.tile],
+        "grid": [Pr, Pc], "frags_per_rank": args.frags, "iters_per_step": args.iters,
+        "inject": args.mode, "swifi_zone": args.zone,
+        "l2": "inputs larger than L2 (A, B, 2 x C per rank = 256 MiB > 126 MB)",
+        "parallelism": f"{Pr}x{Pc} output-tile grid, one rank per GPU",
+    }
+
+
+def peak_hbm():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def verify_traffic_per_launch(tile, frags):
+    """DRAM bytes per verify launch from the committed ncu summary, if one matches this workload."""
+    path = os.path.join(ROOT, "profiles", "verify_traffic.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        key = f"{tile}x{tile // frags}"
+        return d.get(key)
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while the timed region runs."""
+
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x2: "applications_clocks_setting",
+               0x1: "gpu_idle", 0x10: "sync_boost"}
+
+    def __init__(self, torch, device, period=0.02):
+        self.samples, self.reasons, self.maxclk, self.err = [], set(), None, None
+        self.period = period
+        self._stop = threading.Event()
+        self._thr = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            props = torch.cuda.get_device_properties(device)
+            bus = getattr(props, "pci_bus_id", None)
+            dom = getattr(props, "pci_domain_id", 0)
+            dev = getattr(props, "pci_device_id", 0)
+            if bus is not None:
+                self.h = pynvml.nvmlDeviceGetHandleByPciBusId(f"{dom:08x}:{bus:02x}:{dev:02x}.0".encode())
+            else:
+                self.h = pynvml.nvmlDeviceGetHandleByIndex(device.index)
+            self.maxclk = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # no NVML: clocks stay unknown
+            self.nv, self.err = None, str(e)
+
+    def _run(self):
+        fn = getattr(self.nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            self.nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                mask = fn(self.h)
+                for bit, name in self.REASONS.items():
+                    if mask & bit and name != "gpu_idle":
+                        self.reasons.add(name)
+            except Exception as e:
+                self.err = str(e)
+            time.sleep(self.period)
+
+    def start(self):
+        if self.nv is not None:
+            self._thr = threading.Thread(target=self._run, daemon=True)
+            self._thr.start()
+
+    def stop(self):
+        if self._thr is not None:
+            self._stop.set()
+            self._thr.join()
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.maxclk, "reasons": [], "samples": 0,
+                    "note": self.err or "no samples"}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.maxclk,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def cpu_baseline(abft, A, B, counts, offsets, tau, args, budget_s, iters_cap):
+    from oracle import cpu_baseline as cb
+    r = cb.protected_iterations(A, B, counts, offsets, tau, args.mode, args.zone, args.seed_a + args.seed_b, 0,
+                                iters_cap, golden=None, time_budget_s=budget_s)
+    return r, cb.host_threads()
+
+
+def run_reference(args):
+    """CPU arm: the reference's algorithm on the host cores (rank 0 only)."""
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+    if rank != 0:
+        return
+    abft = importlib.import_module(PKG)
+    import numpy as np
+    from oracle import cpu_baseline as cb
+    from oracle import oracle as orc
+    Pr, Pc = abft.choose_grid(max(world, args.gpus))
+    M_b = N_b = args.tile
+    K = args.K
+    A = orc.fill_random(M_b * K, args.seed_a).reshape(M_b, K)
+    B = orc.fill_random(K * N_b, args.seed_b).reshape(K, N_b)
+    counts, offsets = orc.split_dim(N_b, args.frags)
+    tau = np.full(args.frags, abft.relative_threshold(A, B, K))
+    for w in range(args.warmup):
+        cb.protected_iterations(A, B, counts, offsets, tau, args.mode, args.zone, args.seed_a + args.seed_b, 0, 1)
+    secs = flops = 0.0
+    per_step = []
+    for t in range(args.steps):
+        r = cb.protected_iterations(A, B, counts, offsets, tau, args.mode, args.zone,
+                                    args.seed_a + args.seed_b + t * 31337, 0, 1)
+        secs += r["seconds"]
+        flops += r["flops"]
+        per_step.append(r["seconds"] * 1e3)
+    # the grid's ranks are independent tiles: the whole job on one host runs them one after another
+    value = flops / secs / 1e12
+    cores = cb.host_threads()
+    sample = (f"1 protected iteration of one {M_b}x{N_b}x{K} rank tile per step (numpy SGEMM + oracle "
+              f"verification/localisation/correction), {args.steps} steps")
+    line = {
+        "metric": METRIC, "impl": "reference", "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": statistics.median(per_step),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (f64 checksums)",
+        "data": "synthetic uniform[-1,1] (mt19937_64)", "config": workload(args, Pr, Pc),
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def isolated_verify_ms(abft, torch, s, reps=3):
+    """Average time of one verify launch alone on a cold buffer (L2 flushed before each)."""
+    ws = s.ws_handle
+    st = torch.cuda.Stream(device=s.device)
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=s.device)  # 256 MiB > L2
+    times = []
+    with torch.cuda.stream(st):
+        for _ in range(reps):
+            for buf in s.C:
+                for f in range(s.F):
+                    flush.fill_(1.0)
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record(st)
+                    abft.host.call("abft_verify", ws, buf.data_ptr(), buf.stride(0), f, 1e30, 0, -1,
+                                   st.cuda_stream)
+                    e1.record(st)
+                    e1.synchronize()
+                    times.append(e0.elapsed_time(e1))
+    del flush
+    return statistics.median(times)
+
+
+def run_ours(args):
+    import numpy as np
+    import torch
+
+    abft = importlib.import_module(PKG)
+    from importlib import import_module
+    dist_mod = import_module(f"{PKG}.distributed")
+    rank, world, local = dist_mod.init_from_env(timeout_s=300)
+    if world != args.gpus and not (world == 1 and args.gpus == 1):
+        args.gpus = world
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    grid = dist_mod.Grid2D(world, rank)
+    Pr, Pc = grid.Pr, grid.Pc
+    M, N, K = Pr * args.tile, Pc * args.tile, args.K
+
+    A_full = B_full = None
+    tau0 = 0.0
+    if rank == 0:
+        A_h = abft.fill_random(M * K, args.seed_a).reshape(M, K)
+        B_h = abft.fill_random(K * N, args.seed_b).reshape(K, N)
+        tau0 = abft.relative_threshold(A_h, B_h, K)
+        A_full = torch.from_numpy(A_h).to(dev)
+        B_full = torch.from_numpy(B_h).to(dev)
+        del A_h, B_h
+    A, B = dist_mod.distribute_panels(grid, M, K, N, A_full, B_full, dev)
+    del A_full, B_full
+    torch.cuda.synchronize(dev)
+    tau = dist_mod.allreduce([tau0], "sum", dev)[0]
+    t = abft.rank_tile(M, K, N, Pr, Pc, rank, args.frags)
+    s = abft.OnlineSession(A, B, counts=t.counts, offsets=t.offsets, max_iters=args.iters)
+    s.set_tau([tau] * t.F)
+    encode_ms = s.encode()
+    s.baseline(1)
+    torch.cuda.synchronize(dev)
+    golden = s.C[0].clone()
+    if args.mode == "swifi":
+        s.set_golden(golden)  # the reference captures the fault-free C only for SWIFI runs
+    base = args.seed_a + args.seed_b
+
+    for w in range(args.warmup):
+        s.baseline(args.iters)
+        s.online(args.mode, args.zone, base_seed=base + w * 31337, rank=rank, repeats=args.iters)
+
+    def region(fn):
+        dist_mod.barrier(dev)
+        torch.cuda.synchronize(dev)
+        out = [fn(i) for i in range(args.steps)]
+        torch.cuda.synchronize(dev)
+        dist_mod.barrier(dev)
+        return out
+
+    b_ms = region(lambda i: s.baseline(args.iters)[0])
+    sampler = ClockSampler(torch, dev)
+    sampler.start()
+    p_res = region(lambda i: s.online(args.mode, args.zone, base_seed=base + (args.warmup + i) * 31337, rank=rank,
+                                      repeats=args.iters))
+    clocks = sampler.stop()
+    p_ms = [r["device_ms"] for r in p_res]
+    cm = np.sum([r["cm"] for r in p_res], axis=0).tolist()
+    restored = int(sum(r["n_restored"] for r in p_res))
+    launches = int(sum(r["kernel_launches"] for r in p_res))
+
+    # live per-launch verify timing (same loop, CUDA events around each verify on the verify stream)
+    prof = s.online(args.mode, args.zone, base_seed=base, rank=rank, repeats=args.iters, profile=True)
+    iso_ms = isolated_verify_ms(abft, torch, s)
+
+    e2e_ms = []
+    h2d = 4 * (t.M_b * K + K * t.N_b)
+    d2h = 4 * t.M_b * t.N_b + 20
+    if not args.no_e2e:
+        hA = A.cpu().pin_memory()
+        hB = B.cpu().pin_memory()
+        hC = torch.empty((t.M_b, t.N_b), dtype=torch.float32).pin_memory()
+        s.run_host(hA, hB, hC, args.mode, args.zone, base_seed=base, rank=rank, repeats=args.iters)
+        e2e_res = region(lambda i: s.run_host(hA, hB, hC, args.mode, args.zone, base_seed=base + i * 31337,
+                                              rank=rank, repeats=args.iters))
+        e2e_ms = [r["e2e_ms"] for r in e2e_res]
+
+    # max over ranks, per step
+    b_max = dist_mod.allreduce(b_ms, "max", dev)
+    p_max = dist_mod.allreduce(p_ms, "max", dev)
+    e_max = dist_mod.allreduce(e2e_ms, "max", dev) if e2e_ms else []
+    cm_all = dist_mod.allreduce(cm + [restored, launches], "sum", dev)
+    verify_avg = prof["verify_ms_sum"] / max(prof["verify_launches"], 1)
+    v_avg_max = dist_mod.allreduce([verify_avg, iso_ms], "max", dev)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        r, cores = cpu_baseline(abft, A.cpu().numpy(), B.cpu().numpy(), t.counts, t.offsets,
+                                np.full(t.F, tau), args, args.cpu_budget, args.iters)
+        cpu = {"value": r["flops"] / r["seconds"] / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+               "sample": f"{r['iters']} protected iteration(s) of the {t.M_b}x{t.N_b}x{K} tile "
+                         f"(numpy SGEMM + oracle verification/localisation/correction), {r['seconds']:.1f} s"}
+
+    s.close()
+    if rank == 0:
+        flops_step = 2.0 * M * N * K * args.iters
+        total_p = sum(p_max)
+        value = flops_step * args.steps / (total_p * 1e-3) / 1e12
+        base_tf = flops_step * args.steps / (sum(b_max) * 1e-3) / 1e12
+        med_b, med_p = statistics.median(b_max), statistics.median(p_max)
+        N_f = int(max(t.counts))
+        bytes_launch = 4.0 * t.M_b * N_f + 24.0 * N_f
+        peak, peak_kind = peak_hbm()
+        live_gbs = bytes_launch / (v_avg_max[0] * 1e-3) / 1e9 if v_avg_max[0] > 0 else None
+        iso_gbs = bytes_launch / (v_avg_max[1] * 1e-3) / 1e9 if v_avg_max[1] > 0 else None
+        traffic = verify_traffic_per_launch(args.tile, args.frags)
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": total_p / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32 (f64 checksums)",
+            "data": "synthetic uniform[-1,1] (mt19937_64, seeds 123456/987654)",
+            "config": workload(args, Pr, Pc),
+            "overhead_pct": (med_p / med_b - 1.0) * 100.0,
+            "overhead_pct_total": (total_p / sum(b_max) - 1.0) * 100.0,
+            "baseline_tflops": base_tf,
+            "baseline_kind": "unprotected cuBLAS SGEMM, same F fragments (pass_baseline)",
+            "encode_ms": encode_ms,
+            "confusion_matrix": {"TP": int(cm_all[0]), "TN": int(cm_all[1]), "FP": int(cm_all[2]),
+                                 "FN": int(cm_all[3]), "restored": int(cm_all[4])},
+            "roofline": {
+                "kernel": "fused verify (actualRow + detect), one fragment per launch",
+                "bound": "hbm", "achieved": live_gbs, "peak": peak, "unit": "GB/s",
+                "frac": (live_gbs / peak) if live_gbs else None, "traffic": traffic,
+                "peak_kind": f"{peak_kind} hbm_gbs",
+                "bytes_per_launch": bytes_launch,
+                "launch_ms_live": v_avg_max[0],
+                "note": "live = average verify launch in the protected loop (overlapping the SGEMMs); "
+                        "isolated = same kernel alone, L2 flushed",
+                "isolated": {"achieved": iso_gbs, "frac": (iso_gbs / peak) if iso_gbs else None,
+                             "launch_ms": v_avg_max[1]},
+            },
+            "gpu_launches": int(cm_all[5]),
+            "clocks": clocks,
+        }
+        if e_max:
+            line["e2e"] = {"value": flops_step * len(e_max) / (sum(e_max) * 1e-3) / 1e12, "unit": "TFLOP/s",
+                           "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
+                           "ms_per_step": sum(e_max) / len(e_max),
+                           "path": "OnlineSession.run_host -> abft_session_run_host (pinned host in/out)"}
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    dist_mod.shutdown()
+
+
+def main():
+    args = parse()
+    if args.warmup < 3:
+        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

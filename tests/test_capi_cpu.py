@@ -1,0 +1,63 @@
+"""CPU checks of the C ABI: the library loads, exports every symbol that
+include/abft_b200.h declares, and its host helpers reject bad arguments.
+No CUDA call is made."""
+import ctypes
+import re
+
+import numpy as np
+import pytest
+
+
+def declared_functions(header_path):
+    text = open(header_path).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    names = re.findall(r"^[A-Za-z_][\w\s\*]*?\b(abft_\w+)\s*\(", text, flags=re.M)
+    return sorted(set(names))
+
+
+def test_library_exports_every_declared_symbol(abft):
+    names = declared_functions(abft.HEADER_PATH)
+    assert len(names) >= 30
+    lib = ctypes.CDLL(abft.LIB_PATH)
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+    # and the Python binding covers all of them
+    assert sorted(abft.SIGNATURES) == names
+
+
+def test_version_and_error_channel(abft):
+    assert abft.lib.abft_version() >= 10000
+    with pytest.raises(abft.AbftError) as e:
+        abft.split_dim(10, 0)
+    assert "split_dim" in str(e.value)
+    with pytest.raises(abft.AbftError):
+        abft.choose_grid(0)
+    with pytest.raises(abft.AbftError):
+        abft.host.call("abft_injection_plan", 0, 0, 0, 0, 4, None, 1, 0, 31, None, None, None, None)
+
+
+def test_swifi_plan_rejects_bad_zone(abft):
+    counts = np.array([4, 4], np.int32)
+    p = counts.ctypes.data_as(ctypes.POINTER(ctypes.c_int))
+    outs = [ctypes.c_int() for _ in range(4)]
+    rc = abft.lib.abft_injection_plan(1, 0, 0, 2, 8, p, abft.INJECT_SWIFI, 5, 40, *[ctypes.byref(o) for o in outs])
+    assert rc == -1
+
+
+def test_rank_tiles_cover_the_matrix(abft):
+    for world in (1, 2, 4, 8, 6):
+        Pr, Pc = abft.choose_grid(world)
+        M, K, N = 1000, 64, 1030
+        cover = np.zeros((M, N), np.int32)
+        for r in range(world):
+            t = abft.rank_tile(M, K, N, Pr, Pc, r)
+            cover[t.row_off:t.row_off + t.M_b, t.col_off:t.col_off + t.N_b] += 1
+            assert t.F == 4 and sum(t.counts) == t.N_b
+        assert (cover == 1).all()
+
+
+def test_frag_policy(abft):
+    assert abft.frag_count(512, 512, 512, 512, 512, 4) == 1          # small-matrix rule
+    assert abft.frag_count(1024, 1024, 1024, 1024, 1024, 4) == 4
+    assert abft.frag_count(4096, 4096, 4096, 4096, 4096, 4, frag_cap=1 << 20) == 16
+    assert abft.frag_count(4096, 4096, 4096, 4096, 3, 4) == 3          # never more than N_b

@@ -1,0 +1,267 @@
+"""GPU parity of the sm_100a kernels against the CPU oracle, through the C ABI.
+
+Bar: bit-exact. Checksums (colSumA, expectedRow, rowSumB_f, expectedCol_f),
+detected column, rowdiff, located row, corrected C and the counters must equal
+the oracle's restatement of the reference kernels bit for bit.
+"""
+import numpy as np
+import pytest
+
+from gpu_cases import add_fault, flip, product_f64, tiles
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [
+    # M, K, N, F
+    (64, 80, 48, 1),
+    (257, 129, 515, 4),      # uneven fragments, N_f not a multiple of 4 -> scalar path
+    (1100, 300, 1030, 3),
+    (1024, 1024, 1024, 4),   # 1024^3 rank tile, F = 4
+    (33, 7, 9, 2),
+    (2048, 64, 512, 4),
+]
+
+
+@pytest.fixture(scope="module")
+def torch_cuda():
+    import torch
+    assert torch.cuda.is_available(), "GPU tests need CUDA"
+    return torch
+
+
+def to_dev(torch, a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def run_gpu_iteration(abft, torch, A, B, C, counts, offsets, tau, inject_frag, golden=None, localize=True):
+    kern = abft.kernels
+    M, K = A.shape
+    N = B.shape[1]
+    ws = kern.Workspace(M, N, K, counts, offsets, max_iters=1)
+    dA, dB, dC = to_dev(torch, A), to_dev(torch, B), to_dev(torch, C)
+    dG = to_dev(torch, golden) if golden is not None else None
+    kern.encode(ws, dA, dB)
+    ws.reset_counters()
+    for f in range(len(counts)):
+        kern.verify(ws, dC, f, tau[f], injected=(f == inject_frag), it=0)
+        if localize:
+            kern.localize_correct(ws, dC, f, tau[f], injected=(f == inject_frag), golden=dG, it=0)
+    torch.cuda.synchronize()
+    cm, nr = ws.counters()
+    ec, er, rd = ws.read_log(1)
+    sums = ws.read_checksums()
+    out = dC.cpu().numpy()
+    ws.close()
+    return dict(cm=cm, nr=nr, ec=ec[0], er=er[0], rd=rd[0], C=out, sums=sums)
+
+
+def run_oracle_iteration(orc, A, B, C, counts, offsets, tau, inject_frag, golden=None, localize=True):
+    colSumA, expRow, rowSumB, expCol = orc.encode(A, B, counts, offsets)
+    Cc = C.copy()
+    cm, nr, ec, er, rd = orc.verify_iteration(Cc, A, B, counts, offsets, expRow, tau, inject_frag, localize,
+                                              expCol=expCol, golden=golden)
+    return dict(cm=cm, nr=nr, ec=ec, er=er, rd=rd, C=Cc, sums=(colSumA, expRow, rowSumB, expCol))
+
+
+def assert_same(g, o):
+    assert list(g["cm"]) == list(o["cm"])
+    assert g["nr"] == o["nr"]
+    assert list(g["ec"]) == list(o["ec"])
+    assert list(g["er"]) == list(o["er"])
+    assert g["rd"].view(np.uint64).tolist() == o["rd"].view(np.uint64).tolist()
+    assert np.array_equal(g["C"].view(np.uint32), o["C"].view(np.uint32))
+
+
+@pytest.mark.parametrize("shape", SHAPES)
+def test_encode_bit_exact(shape, abft, orc, torch_cuda):
+    M, K, N, F = shape
+    A, B = tiles(orc, M, K, N)
+    counts, offsets = orc.split_dim(N, F)
+    C = product_f64(A, B)
+    g = run_gpu_iteration(abft, torch_cuda, A, B, C, counts, offsets, [1e30] * F, -1, localize=False)
+    o = orc.encode(A, B, counts, offsets)
+    for got, want, name in zip(g["sums"], o, ["colSumA", "expRow", "rowSumB", "expCol"]):
+        assert np.array_equal(got.view(np.uint64), want.view(np.uint64)), name
+
+
+def test_encode_strided_and_unaligned(abft, orc, torch_cuda):
+    """Tiles that are views: leading dimensions larger than the width, base not 16-byte aligned."""
+    torch = torch_cuda
+    M, K, N, F = 300, 200, 260, 3
+    Aw, Bw = tiles(orc, M, K + 7, N + 5, 11, 12)
+    counts, offsets = orc.split_dim(N, F)
+    dAw, dBw = to_dev(torch, Aw), to_dev(torch, Bw)
+    dA, dB = dAw[:, 1:K + 1], dBw[:, 3:N + 3]
+    A, B = Aw[:, 1:K + 1], Bw[:, 3:N + 3]
+    ws = abft.kernels.Workspace(M, N, K, counts, offsets)
+    abft.kernels.encode(ws, dA, dB)
+    torch.cuda.synchronize()
+    got = ws.read_checksums()
+    want = orc.encode(A, B, counts, offsets)
+    for g, w in zip(got, want):
+        assert np.array_equal(g.view(np.uint64), w.view(np.uint64))
+
+
+@pytest.mark.parametrize("shape", SHAPES)
+def test_clean_tile_no_detection(shape, abft, orc, torch_cuda):
+    M, K, N, F = shape
+    A, B = tiles(orc, M, K, N, 3, 4)
+    counts, offsets = orc.split_dim(N, F)
+    C = product_f64(A, B)
+    tau = [1e-5 * K] * F
+    g = run_gpu_iteration(abft, torch_cuda, A, B, C, counts, offsets, tau, -1)
+    o = run_oracle_iteration(orc, A, B, C, counts, offsets, tau, -1)
+    assert_same(g, o)
+
+
+@pytest.mark.parametrize("shape", SHAPES)
+def test_additive_fault_every_fragment(shape, abft, orc, torch_cuda):
+    M, K, N, F = shape
+    A, B = tiles(orc, M, K, N, 5, 6)
+    counts, offsets = orc.split_dim(N, F)
+    C0 = product_f64(A, B)
+    rng = np.random.default_rng(1)
+    for f in range(F):
+        r = int(rng.integers(0, M))
+        c = int(offsets[f] + rng.integers(0, counts[f]))
+        for delta in (1.0e6, 1.0, 0.03125):
+            C = add_fault(C0, r, c, delta)
+            tau = [1e-5 * K] * F
+            g = run_gpu_iteration(abft, torch_cuda, A, B, C, counts, offsets, tau, f, golden=C0)
+            o = run_oracle_iteration(orc, A, B, C, counts, offsets, tau, f, golden=C0)
+            assert_same(g, o)
+
+
+@pytest.mark.parametrize("shape", [(257, 129, 515, 4), (1024, 1024, 1024, 4)])
+def test_bitflips_all_bits(shape, abft, orc, torch_cuda):
+    M, K, N, F = shape
+    A, B = tiles(orc, M, K, N, 7, 8)
+    counts, offsets = orc.split_dim(N, F)
+    C0 = product_f64(A, B)
+    rng = np.random.default_rng(2)
+    tau = [1e-5 * K] * F
+    for bit in range(32):
+        f = int(rng.integers(0, F))
+        r = int(rng.integers(0, M))
+        c = int(offsets[f] + rng.integers(0, counts[f]))
+        C = flip(C0, r, c, bit)
+        g = run_gpu_iteration(abft, torch_cuda, A, B, C, counts, offsets, tau, f, golden=C0)
+        o = run_oracle_iteration(orc, A, B, C, counts, offsets, tau, f, golden=C0)
+        assert_same(g, o)
+
+
+@pytest.mark.parametrize("shape", [(257, 129, 515, 4), (1024, 1024, 1024, 4), (2048, 64, 512, 4)])
+def test_zero_threshold_noise_argmax(shape, abft, orc, torch_cuda):
+    """tau = 0: every noisy column is a candidate; the arg-max over pure rounding
+    noise must still be the reference's (exact values, exact tie rule)."""
+    M, K, N, F = shape
+    A, B = tiles(orc, M, K, N, 9, 10)
+    counts, offsets = orc.split_dim(N, F)
+    C = product_f64(A, B)
+    tau = [0.0] * F
+    g = run_gpu_iteration(abft, torch_cuda, A, B, C, counts, offsets, tau, -1)
+    o = run_oracle_iteration(orc, A, B, C, counts, offsets, tau, -1)
+    assert_same(g, o)
+
+
+def test_exact_ties(abft, orc, torch_cuda):
+    """A = 0 makes every expected checksum 0, so equal faults give exactly equal
+    |actual - expected|: the winner is decided by the reference's tree rule."""
+    M, K, N, F = 600, 16, 1030, 2
+    A = np.zeros((M, K), np.float32)
+    _, B = tiles(orc, M, K, N)
+    counts, offsets = orc.split_dim(N, F)
+    for cols in ([1, 2, 3], [0, 256, 257, 513], [5, 261, 517], [255, 511, 300, 44]):
+        C = np.zeros((M, N), np.float32)
+        for k, c in enumerate(cols):
+            C[(7 * k + 3) % M, c] = 3.0
+            C[(7 * k + 3) % M, offsets[1] + c % counts[1]] = 3.0
+        tau = [0.5] * F
+        g = run_gpu_iteration(abft, torch_cuda, A, B, C, counts, offsets, tau, 0)
+        o = run_oracle_iteration(orc, A, B, C, counts, offsets, tau, 0)
+        assert_same(g, o)
+
+
+def test_uncertified_sum_uses_sequential_value(abft, orc, torch_cuda):
+    """Columns whose parallel double sum differs from the sequential one:
+    2^30 followed by many 2^-27 terms. Each sequential add rounds the small
+    term away; a parallel partial of 16 or more small terms survives."""
+    M, K, N, F = 4096, 8, 256, 1
+    A = np.zeros((M, K), np.float32)
+    _, B = tiles(orc, M, K, N)
+    counts, offsets = orc.split_dim(N, F)
+    C = np.zeros((M, N), np.float32)
+    C[0, 17] = 2.0 ** 30
+    C[1:, 17] = 2.0 ** -27
+    C[5, 40] = 2.0 ** 29
+    C[6:, 40] = 2.0 ** -28
+    seq = orc.actual_row(C)
+    assert seq[17] == 2.0 ** 30 and seq[40] == 2.0 ** 29  # the reference's values
+    assert float(C[:, 17].astype(np.float64).sum()) != 2.0 ** 30  # an unordered sum differs
+    for tau in (0.5, 2.0 ** 30 + 2.0 ** -22, 2.0 ** 29 + 1.0):
+        g = run_gpu_iteration(abft, torch_cuda, A, B, C, counts, offsets, [tau], 0)
+        o = run_oracle_iteration(orc, A, B, C, counts, offsets, [tau], 0)
+        assert_same(g, o)
+
+
+def test_nonfinite_values(abft, orc, torch_cuda):
+    M, K, N, F = 512, 32, 384, 3
+    A, B = tiles(orc, M, K, N, 13, 14)
+    counts, offsets = orc.split_dim(N, F)
+    C0 = product_f64(A, B)
+    tau = [1e-3] * F
+    for val in (np.inf, -np.inf, np.nan, 3.0e38):
+        for f in range(F):
+            C = C0.copy()
+            C[100, offsets[f] + 5] = val
+            g = run_gpu_iteration(abft, torch_cuda, A, B, C, counts, offsets, tau, f, golden=C0)
+            o = run_oracle_iteration(orc, A, B, C, counts, offsets, tau, f, golden=C0)
+            assert_same(g, o)
+    C = C0.copy()
+    C[3, 4] = np.inf
+    C[9, 4] = -np.inf
+    g = run_gpu_iteration(abft, torch_cuda, A, B, C, counts, offsets, tau, 0, golden=C0)
+    o = run_oracle_iteration(orc, A, B, C, counts, offsets, tau, 0, golden=C0)
+    assert_same(g, o)
+
+
+def test_multiple_faults_one_fragment(abft, orc, torch_cuda):
+    """Two faults in one fragment (outside the single-fault model): decisions
+    still follow the reference exactly."""
+    M, K, N, F = 1024, 256, 1024, 4
+    A, B = tiles(orc, M, K, N, 15, 16)
+    counts, offsets = orc.split_dim(N, F)
+    C0 = product_f64(A, B)
+    C = add_fault(add_fault(C0, 10, 20, 5.0), 700, 20, 6.0)
+    C = add_fault(C, 11, 100, 5.5)
+    tau = [1e-5 * K] * F
+    g = run_gpu_iteration(abft, torch_cuda, A, B, C, counts, offsets, tau, 0, golden=C0)
+    o = run_oracle_iteration(orc, A, B, C, counts, offsets, tau, 0, golden=C0)
+    assert_same(g, o)
+
+
+def test_injectors(abft, torch_cuda):
+    torch = torch_cuda
+    C = torch.zeros((8, 12), dtype=torch.float32, device="cuda")
+    C[3, 5] = 1.5
+    abft.kernels.inject_add(C, 3, 5, 1.0e6)
+    abft.kernels.inject_bitflip(C, 2, 7, 30)
+    torch.cuda.synchronize()
+    h = C.cpu().numpy()
+    assert h[3, 5] == np.float32(np.float32(1.5) + np.float32(1.0e6))
+    assert h[2, 7].view(np.uint32) == np.uint32(1 << 30)
+
+
+def test_bad_arguments_raise(abft, torch_cuda):
+    torch = torch_cuda
+    with pytest.raises(abft.AbftError):
+        abft.kernels.Workspace(0, 4, 4, [4], [0])
+    with pytest.raises(abft.AbftError):
+        abft.kernels.Workspace(4, 4, 4, [3, 3], [0, 3])  # fragment beyond the tile
+    ws = abft.kernels.Workspace(4, 4, 4, [4], [0])
+    C = torch.zeros((4, 4), device="cuda")
+    with pytest.raises(abft.AbftError):
+        abft.kernels.verify(ws, C, 1, 1.0)  # fragment index out of range
+    with pytest.raises(abft.AbftError):
+        abft.kernels.inject_bitflip(C, 0, 0, 32)
+    ws.close()

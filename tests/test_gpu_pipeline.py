@@ -1,0 +1,133 @@
+"""GPU parity of the online pipeline (pass_online_loop) against the oracle.
+
+The SGEMM is cuBLAS on the GPU; the oracle replays the reference's decision
+path on the GPU's own fault-free C (every iteration recomputes the same C), so
+every decision, counter, injection and final buffer must be bit-identical.
+"""
+import numpy as np
+import pytest
+import torch
+
+from gpu_cases import tiles
+
+pytestmark = pytest.mark.gpu
+
+
+def make_session(abft, orc, M, K, N, F, seed_a=123456, seed_b=987654, tau=None, max_iters=64, dist="uniform"):
+    A, B = tiles(orc, M, K, N, seed_a, seed_b, dist)
+    counts, offsets = orc.split_dim(N, F)
+    s = abft.OnlineSession(torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda(), counts=counts, offsets=offsets,
+                           max_iters=max_iters)
+    if tau is None:
+        tau = [abft.relative_threshold(A, B, K)] * F
+    s.set_tau(tau)
+    s.baseline(1)
+    torch.cuda.synchronize()
+    C_clean = s.C[0].cpu().numpy().copy()
+    return s, A, B, counts, offsets, np.asarray(s.tau), C_clean
+
+
+def compare(s, res, o, repeats, check_injections=True):
+    assert res["cm"] == list(o["cm"])
+    assert res["n_restored"] == o["n_restored"]
+    n = min(repeats, s.max_iters)
+    ec, er, rd = s.read_log(n)
+    assert np.array_equal(ec, o["errcol"][:n])
+    assert np.array_equal(er, o["errrow"][:n])
+    assert np.array_equal(rd.view(np.uint64), o["rowdiff"][:n].view(np.uint64))
+    if check_injections:
+        inj, _ = s.read_injections(n)
+        want = o["inj"][:n].copy()
+        assert np.array_equal(inj[want[:, 0] >= 0], want[want[:, 0] >= 0])
+    torch.cuda.synchronize()
+    assert np.array_equal(s.C[0].cpu().numpy().view(np.uint32), o["buf0"].view(np.uint32))
+    if repeats > 1:
+        assert np.array_equal(s.C[1].cpu().numpy().view(np.uint32), o["buf1"].view(np.uint32))
+
+
+@pytest.mark.parametrize("mode,zone", [("none", "any"), ("add", "any"), ("swifi", "any"), ("swifi", "exponent"),
+                                       ("swifi", "sig_low"), ("swifi", "sign"), ("swifi", "sig_high")])
+def test_online_1024_cube(mode, zone, abft, orc):
+    """1024^3, F = 4, 10 iterations (the single-rank 1024^3 workload)."""
+    s, A, B, counts, offsets, tau, C0 = make_session(abft, orc, 1024, 1024, 1024, 4)
+    golden = torch.from_numpy(C0).cuda() if mode == "swifi" else None
+    s.set_golden(golden)
+    base = 123456 + 987654 + 2 * 31337
+    res = s.online(mode, zone, base_seed=base, repeats=10, log=True)
+    o = orc.online_loop(C0, A, B, counts, offsets, tau, mode, zone, 1.0e6, base, 0, 10,
+                        golden=C0 if mode == "swifi" else None)
+    compare(s, res, o, 10)
+    if mode == "add":
+        assert res["cm"][0] == 10 and res["cm"][3] == 0  # every additive fault detected
+    s.close()
+
+
+@pytest.mark.parametrize("correct", ["inloop", "drain"])
+def test_drain_equals_inloop(correct, abft, orc):
+    s, A, B, counts, offsets, tau, C0 = make_session(abft, orc, 512, 384, 768, 4, 1, 2)
+    s.set_golden(torch.from_numpy(C0).cuda())
+    res = s.online("swifi", "exponent", base_seed=99, repeats=9, log=True, correct=correct)
+    o = orc.online_loop(C0, A, B, counts, offsets, tau, "swifi", "exponent", 1.0e6, 99, 0, 9, golden=C0)
+    compare(s, res, o, 9)
+    s.close()
+
+
+def test_uneven_fragments_and_rank(abft, orc):
+    s, A, B, counts, offsets, tau, C0 = make_session(abft, orc, 1100, 300, 1030, 3, 5, 7)
+    s.set_golden(torch.from_numpy(C0).cuda())
+    res = s.online("swifi", "any", base_seed=4242, rank=5, repeats=12, log=True)
+    o = orc.online_loop(C0, A, B, counts, offsets, tau, "swifi", "any", 1.0e6, 4242, 5, 12, golden=C0)
+    compare(s, res, o, 12)
+    s.close()
+
+
+def test_formula_threshold_and_normal_inputs(abft, orc):
+    """Reference default threshold (gamma_K formula) and normal(0,1) inputs."""
+    M, K, N, F = 2048, 1024, 1024, 4
+    A, B = tiles(orc, M, K, N, 21, 22, "normal")
+    counts, offsets = orc.split_dim(N, F)
+    tau = abft.frag_thresholds(A, B, counts, offsets)
+    s, A, B, counts, offsets, tau, C0 = make_session(abft, orc, M, K, N, F, 21, 22, tau=tau, dist="normal")
+    res = s.online("add", base_seed=7, repeats=6, log=True)
+    o = orc.online_loop(C0, A, B, counts, offsets, tau, "add", "any", 1.0e6, 7, 0, 6)
+    compare(s, res, o, 6)
+    s.close()
+
+
+def test_add_delta_one_restores_clean_c(abft, orc):
+    """+1.0 faults (the 1024^3 workload's fault size) with a golden C: every
+    fault is detected, located and corrected back to within tau of the
+    fault-free value, bit-identically to the oracle."""
+    s, A, B, counts, offsets, tau, C0 = make_session(abft, orc, 1024, 1024, 1024, 4, 0, 0)
+    s.set_golden(torch.from_numpy(C0).cuda())
+    res = s.online("add", add_delta=1.0, base_seed=1, repeats=10, log=True)
+    o = orc.online_loop(C0, A, B, counts, offsets, tau, "add", "any", 1.0, 1, 0, 10, golden=C0)
+    compare(s, res, o, 10)
+    assert res["cm"][0] == 10 and res["n_restored"] == 10
+    torch.cuda.synchronize()
+    err = np.abs(s.C[1].cpu().numpy().astype(np.float64) - C0).max() / np.abs(C0).max()
+    assert err <= 1e-5
+    s.close()
+
+
+def test_repeats_beyond_log_capacity(abft, orc):
+    s, A, B, counts, offsets, tau, C0 = make_session(abft, orc, 256, 256, 512, 4, max_iters=4)
+    res = s.online("add", base_seed=3, repeats=11, log=True)
+    o = orc.online_loop(C0, A, B, counts, offsets, tau, "add", "any", 1.0e6, 3, 0, 11)
+    compare(s, res, o, 11)
+    s.close()
+
+
+def test_baseline_and_run_host(abft, orc):
+    s, A, B, counts, offsets, tau, C0 = make_session(abft, orc, 768, 512, 1024, 4, 31, 32)
+    ms, hms = s.baseline(3)
+    assert ms > 0 and hms > 0
+    hA = torch.from_numpy(A).pin_memory()
+    hB = torch.from_numpy(B).pin_memory()
+    hC = torch.empty((768, 1024), dtype=torch.float32).pin_memory()
+    res = s.run_host(hA, hB, hC, "add", base_seed=17, repeats=3)
+    o = orc.online_loop(C0, A, B, counts, offsets, tau, "add", "any", 1.0e6, 17, 0, 3)
+    assert res["cm"] == list(o["cm"])
+    assert np.array_equal(hC.numpy().view(np.uint32), o["buf0"].view(np.uint32))
+    assert res["e2e_ms"] > 0
+    s.close()
