@@ -61,6 +61,30 @@ class OnlineResult(ctypes.Structure):
     ]
 
 
+class Timing(ctypes.Structure):
+    _fields_ = [("min_ms", ctypes.c_double), ("median_ms", ctypes.c_double), ("mean_ms", ctypes.c_double),
+                ("max_ms", ctypes.c_double), ("n_samples", ctypes.c_int)]
+
+
+class Metrics(ctypes.Structure):
+    _fields_ = [
+        ("scheme", ctypes.c_char * 16), ("inject", ctypes.c_char * 16), ("swifi_zone", ctypes.c_char * 16),
+        ("baseline_only", ctypes.c_int), ("calibrate", ctypes.c_int),
+        ("M", ctypes.c_int), ("K", ctypes.c_int), ("N", ctypes.c_int), ("Pr", ctypes.c_int), ("Pc", ctypes.c_int),
+        ("frags_per_rank", ctypes.c_int), ("num_fragments_total", ctypes.c_int), ("repeats", ctypes.c_int),
+        ("threshold_used", ctypes.c_double), ("baseline", Timing), ("protected_", Timing),
+        ("cm", ctypes.c_int * 4), ("n_restored", ctypes.c_int),
+        ("calib_max_diff", ctypes.c_double), ("calib_safety_factor", ctypes.c_double),
+        ("calib_suggested_tau", ctypes.c_double),
+        ("overhead_pct", ctypes.c_double), ("recall", ctypes.c_double), ("precision", ctypes.c_double),
+        ("correction_precision_pct", ctypes.c_double),
+        ("baseline_gflops_min", ctypes.c_double), ("baseline_gflops_median", ctypes.c_double),
+        ("baseline_gflops_mean", ctypes.c_double), ("baseline_gflops_max", ctypes.c_double),
+        ("protected_gflops_min", ctypes.c_double), ("protected_gflops_median", ctypes.c_double),
+        ("protected_gflops_mean", ctypes.c_double), ("protected_gflops_max", ctypes.c_double),
+    ]
+
+
 _P = ctypes.c_void_p
 _I = ctypes.c_int
 _I64 = ctypes.c_int64
@@ -109,6 +133,10 @@ SIGNATURES = {
     "abft_session_read_injections": (_I, [_P, _I, _IP, ctypes.POINTER(ctypes.c_float)]),
     "abft_session_run_host": (_I, [_P, _P, _P, _P, ctypes.POINTER(OnlineArgs), ctypes.POINTER(OnlineResult),
                                    _DP]),
+    "abft_stats_of": (_I, [_DP, _I, ctypes.POINTER(Timing)]),
+    "abft_metrics_finalize": (_I, [ctypes.POINTER(Metrics)]),
+    "abft_metrics_report": (_I, [ctypes.POINTER(Metrics), ctypes.c_char_p, ctypes.c_size_t]),
+    "abft_metrics_csv_append": (_I, [ctypes.POINTER(Metrics), ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p]),
 }
 
 

@@ -27,8 +27,8 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 HOST_FLAGS = "-fPIC,-ffp-contract=off,-O2"
 
 LIB_CU = ["abft_kernels.cu", "abft_capi.cu", "abft_pipeline.cu"]
-LIB_CPP = ["abft_host.cpp"]
-DRIVER_SRC = ["abft_gemm_main.cpp", "abft_report.cpp", "abft_comm.cpp"]
+LIB_CPP = ["abft_host.cpp", "abft_report.cpp"]
+DRIVER_SRC = ["abft_gemm_main.cpp", "abft_comm.cpp"]
 
 
 def _run(cmd):

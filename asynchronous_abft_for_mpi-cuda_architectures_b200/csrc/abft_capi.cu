@@ -41,7 +41,9 @@ WsLayout ws_layout(int M_b, int N_b, int K, int F, int nfmax, int max_iters) {
     L.expCol = take(sizeof(double) * (size_t)F * M_b);
     L.rec = take(sizeof(FragRecord) * F);
     L.ctr = take(sizeof(Counters));
-    L.vpart = take(sizeof(ColPartial) * kMaxChunks * nfpad);
+    L.vacc_s = take(sizeof(double) * nfpad);
+    L.vacc_t = take(sizeof(float) * nfpad);
+    L.vacc_m = take(sizeof(uint32_t) * nfpad);
     L.vact = take(sizeof(double) * nfpad);
     L.vd = take(sizeof(double) * nfpad);
     L.vw = take(sizeof(double) * nfpad);
@@ -146,6 +148,12 @@ int abft_ws_create(int M_b, int N_b, int K, int F, const int* counts, const int*
         return cuda_fail(e, "workspace memset");
     }
     char* b = static_cast<char*>(ws->base);
+    e = cudaMemset(b + L.vacc_m, 0xff, sizeof(uint32_t) * ws->nfpad);
+    if (e != cudaSuccess) {
+        if (ws->owns) cudaFree(ws->base);
+        delete ws;
+        return cuda_fail(e, "workspace memset");
+    }
     WsDev& d = ws->d;
     d.colSumA = reinterpret_cast<double*>(b + L.colSumA);
     d.expRow = reinterpret_cast<double*>(b + L.expRow);
@@ -153,7 +161,9 @@ int abft_ws_create(int M_b, int N_b, int K, int F, const int* counts, const int*
     d.expCol = reinterpret_cast<double*>(b + L.expCol);
     d.rec = reinterpret_cast<FragRecord*>(b + L.rec);
     d.ctr = reinterpret_cast<Counters*>(b + L.ctr);
-    d.vpart = reinterpret_cast<ColPartial*>(b + L.vpart);
+    d.vacc_s = reinterpret_cast<double*>(b + L.vacc_s);
+    d.vacc_t = reinterpret_cast<float*>(b + L.vacc_t);
+    d.vacc_m = reinterpret_cast<uint32_t*>(b + L.vacc_m);
     d.vact = reinterpret_cast<double*>(b + L.vact);
     d.vd = reinterpret_cast<double*>(b + L.vd);
     d.vw = reinterpret_cast<double*>(b + L.vw);

@@ -12,15 +12,8 @@ namespace abft {
 constexpr int kThreads = 256;    // threads of the verify / localise CTAs
 constexpr int kWarps = kThreads / 32;
 constexpr int kGroupCols = 128;  // columns per verify CTA: 32 lanes x 4 columns
-constexpr int kMaxChunks = 64;   // row chunks per column group (verify partials)
-
-// One row-chunk partial of a column: double sum, float sum of |x| and the
-// smallest (|x| bits - 1) (unsigned; 0xffffffff when every term is zero).
-struct ColPartial {
-    double s;
-    float t;
-    uint32_t mbm1;
-};
+constexpr int kMaxChunks = 1024; // row chunks per column group (verify grid.y)
+constexpr int kVerifySmemMax = 64 * 1024;  // verify dynamic shared memory cap
 
 // Per-fragment decision record (the reference's dErrCol[f] / dRowDiff[f],
 // plus the located row).
@@ -64,7 +57,11 @@ struct WsDev {
     double* expCol;    // [F][M_b]
     FragRecord* rec;   // [F]
     Counters* ctr;
-    ColPartial* vpart; // [kMaxChunks][nfpad]
+    // per-column accumulators of the verify kernel: double sum, float sum of
+    // |x| and the smallest (|x| bits - 1) (0xffffffff when every term is 0)
+    double* vacc_s;    // [nfpad]
+    float* vacc_t;     // [nfpad]
+    uint32_t* vacc_m;  // [nfpad]
     double* vact;      // [nfpad]
     double* vd;
     double* vw;
@@ -99,7 +96,7 @@ void set_error(const std::string& msg);
 int cuda_fail(cudaError_t e, const char* what);
 
 struct WsLayout {
-    size_t colSumA, expRow, rowSumB, expCol, rec, ctr, vpart, vact, vd, vw, vcnt, lact, ld, lw, lcnt, dlog, ilog,
+    size_t colSumA, expRow, rowSumB, expCol, rec, ctr, vacc_s, vacc_t, vacc_m, vact, vd, vw, vcnt, lact, ld, lw, lcnt, dlog, ilog,
         pend, total;
 };
 WsLayout ws_layout(int M_b, int N_b, int K, int F, int nfmax, int max_iters);

@@ -28,6 +28,10 @@
 #include <math.h>
 #include <stdint.h>
 
+#include <algorithm>
+#include <mutex>
+#include <set>
+
 #include "abft_b200.h"
 #include "abft_internal.h"
 
@@ -36,20 +40,9 @@ namespace {
 
 constexpr unsigned kFull = 0xffffffffu;
 constexpr int kListCap = 256;
+constexpr int kBatch = 16;  // rows in flight per warp in the verify body
 
 // ------------------------------------------------------------- helpers ----
-
-__device__ __forceinline__ double2 pack_partial(double s, float t, uint32_t mbm1) {
-    unsigned long long hi = ((unsigned long long)mbm1 << 32) | (unsigned long long)__float_as_uint(t);
-    return make_double2(s, __longlong_as_double((long long)hi));
-}
-
-__device__ __forceinline__ void unpack_partial(double2 p, double& s, float& t, uint32_t& mbm1) {
-    s = p.x;
-    unsigned long long hi = (unsigned long long)__double_as_longlong(p.y);
-    t = __uint_as_float((uint32_t)(hi & 0xffffffffull));
-    mbm1 = (uint32_t)(hi >> 32);
-}
 
 // Window w >= 0 with |d_reference - d| <= w for a sum S of n float terms with
 // float |x|-sum T and smallest (|x| bits - 1) mbm1; w == 0 means S (and so d)
@@ -107,18 +100,27 @@ struct SelectSmem {
     int flag;
 };
 
+// Loads of the arg-max inputs: CG = written by other CTAs of this grid (read
+// through L2), otherwise written by this CTA (shared or global memory).
+template <bool CG>
+__device__ __forceinline__ double ld_sel(const double* p) {
+    if (CG) return __ldcg(p);
+    return *p;
+}
+
 // Arg-max of k_detect_row / k_locate_correct (kernels/abft_stepwise.cuh:85-110,
 // :174-187) over n entries, run by one 256-thread CTA. act/dd/ww hold the fast
 // sum, its |act - exp| and window; entries that could change the outcome are
 // first re-summed exactly by `exact(j)` (warp-cooperative). Returns the
 // reference's winner or -1.
-template <class Exact>
+template <bool CG, class Exact>
 __device__ int final_select(int n, double tau, const double* __restrict__ expv, double* act, double* dd, double* ww,
                             Exact exact, SelectSmem& sm) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     double bc = -INFINITY;
+#pragma unroll 4
     for (int j = tid; j < n; j += kThreads) {
-        const double wv = __ldcg(ww + j), dv = __ldcg(dd + j);
+        const double wv = ld_sel<CG>(ww + j), dv = ld_sel<CG>(dd + j);
         if (wv == 0.0 && dv > tau && dv > bc) bc = dv;
     }
     sm.d[tid] = bc;
@@ -133,10 +135,11 @@ __device__ int final_select(int n, double tau, const double* __restrict__ expv, 
     for (;;) {
         if (tid == 0) sm.cnt = 0;
         __syncthreads();
+#pragma unroll 4
         for (int j = tid; j < n; j += kThreads) {
-            const double wv = __ldcg(ww + j);
+            const double wv = ld_sel<CG>(ww + j);
             if (wv != 0.0) {
-                const double hi = __ldcg(dd + j) + wv;
+                const double hi = ld_sel<CG>(dd + j) + wv;
                 if (hi > tau && hi >= best_cert) {
                     const int k = atomicAdd(&sm.cnt, 1);
                     if (k < kListCap) sm.list[k] = j;
@@ -161,9 +164,10 @@ __device__ int final_select(int n, double tau, const double* __restrict__ expv, 
 
     double best = 0.0;
     int bj = -1;
+#pragma unroll 4
     for (int j = tid; j < n; j += kThreads) {
-        if (__ldcg(ww + j) == 0.0) {
-            const double dv = __ldcg(dd + j);
+        if (ld_sel<CG>(ww + j) == 0.0) {
+            const double dv = ld_sel<CG>(dd + j);
             if (dv > tau && dv > best) {
                 best = dv;
                 bj = j;
@@ -188,17 +192,22 @@ __device__ int final_select(int n, double tau, const double* __restrict__ expv, 
 // ------------------------------------------------------------- verify -----
 
 // Fused actualRow + detect for one fragment (M x N, leading dimension ldc).
-// grid = (groups of 128 columns, row chunks). Each CTA reduces its tile into
-// per-column partials; the last CTA of a column group folds the partials and
-// certifies each column; the last group runs the reference's arg-max.
+// grid = (groups of 128 columns, row chunks). Each CTA streams its tile with
+// 128-bit loads, reduces it to per-column (sum, |x|-sum, smallest |x|) and
+// adds those into per-column accumulators with device atomics (any order:
+// certified sums are exact in every order, uncertified ones carry a window
+// valid for every order). The last CTA to finish certifies each column and
+// runs the reference's arg-max. Shared memory: 16 KB for the CTA reduction,
+// reused by the last CTA for the d / w arrays when 16*N bytes fit.
 template <bool VEC>
 __global__ void __launch_bounds__(kThreads)
-    k_verify(const float* __restrict__ C, long long ldc, int M, int N, int rows_per, int chunks, int groups,
-             int nfpad, const double* __restrict__ expv, double tau, int injected, int f, int F, int it, WsDev w) {
-    __shared__ double s_s[kWarps][kGroupCols];
-    __shared__ float s_t[kWarps][kGroupCols];
-    __shared__ uint32_t s_m[kWarps][kGroupCols];
+    k_verify(const float* __restrict__ C, long long ldc, int M, int N, int rows_per, int total_ctas, int dw_in_smem,
+             const double* __restrict__ expv, double tau, int injected, int f, int F, int it, WsDev w) {
+    extern __shared__ __align__(16) unsigned char dsm[];
     __shared__ SelectSmem sel;
+    double(*s_s)[kGroupCols] = reinterpret_cast<double(*)[kGroupCols]>(dsm);
+    float(*s_t)[kGroupCols] = reinterpret_cast<float(*)[kGroupCols]>(dsm + kWarps * kGroupCols * 8);
+    uint32_t(*s_m)[kGroupCols] = reinterpret_cast<uint32_t(*)[kGroupCols]>(dsm + kWarps * kGroupCols * 12);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = blockIdx.x, chunk = blockIdx.y;
@@ -231,15 +240,18 @@ __global__ void __launch_bounds__(kThreads)
         acc1(v.w, s3, t3, m3);
     };
 
-    int r = r0 + warp;
-    for (; r + 7 * kWarps < r1; r += 8 * kWarps) {
-        float4 v[8];
+    // Batches of kBatch rows per warp, predicated, so that every load of a
+    // batch is in flight at once (one memory latency per batch).
+    for (int r = r0 + warp; r < r1; r += kBatch * kWarps) {
+        float4 v[kBatch];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) v[u] = load(r + u * kWarps);
+        for (int u = 0; u < kBatch; ++u) {
+            const int rr = r + u * kWarps;
+            v[u] = (rr < r1) ? load(rr) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
 #pragma unroll
-        for (int u = 0; u < 8; ++u) acc(v[u]);
+        for (int u = 0; u < kBatch; ++u) acc(v[u]);
     }
-    for (; r < r1; r += kWarps) acc(load(r));
 
     const int cl = lane * 4;
     s_s[warp][cl + 0] = s0; s_s[warp][cl + 1] = s1; s_s[warp][cl + 2] = s2; s_s[warp][cl + 3] = s3;
@@ -258,52 +270,41 @@ __global__ void __launch_bounds__(kThreads)
                 T += s_t[k][tid];
                 mb = min(mb, s_m[k][tid]);
             }
-            reinterpret_cast<double2*>(w.vpart)[(long long)chunk * nfpad + col] = pack_partial(S, T, mb);
+            atomicAdd(w.vacc_s + col, S);
+            atomicAdd(w.vacc_t + col, T);
+            atomicMin(w.vacc_m + col, mb);
         }
     }
     __threadfence();
     __syncthreads();
-    if (tid == 0) sel.flag = (atomicAdd(&w.vcnt[g], 1) == chunks - 1);
+    if (tid == 0) sel.flag = (atomicAdd(w.vcnt, 1) == total_ctas - 1);
     __syncthreads();
     if (!sel.flag) return;
     __threadfence();
 
-    // Last CTA of column group g: fold the row-chunk partials in chunk order.
-    if (tid < kGroupCols) {
-        const int col = g * kGroupCols + tid;
-        if (col < N) {
-            double S = 0.0;
-            float T = 0.f;
-            uint32_t mb = kFull;
-            const double2* pp = reinterpret_cast<const double2*>(w.vpart);
-            for (int ch = 0; ch < chunks; ++ch) {
-                double ps;
-                float pt;
-                uint32_t pm;
-                unpack_partial(__ldcg(pp + (long long)ch * nfpad + col), ps, pt, pm);
-                S = __dadd_rn(S, ps);
-                T += pt;
-                mb = min(mb, pm);
-            }
-            const double d = fabs(S - expv[col]);
-            w.vact[col] = S;
-            w.vd[col] = d;
-            w.vw[col] = cert_window(S, T, mb, M, d);
-        }
+    // Last CTA: certify every column, reset the accumulators for the next launch.
+    double* dd = dw_in_smem ? reinterpret_cast<double*>(dsm) : w.vd;
+    double* ww = dw_in_smem ? reinterpret_cast<double*>(dsm) + N : w.vw;
+#pragma unroll 4
+    for (int j = tid; j < N; j += kThreads) {
+        const double S = __ldcg(w.vacc_s + j);
+        const float T = __ldcg(w.vacc_t + j);
+        const uint32_t mb = __ldcg(w.vacc_m + j);
+        w.vacc_s[j] = 0.0;
+        w.vacc_t[j] = 0.f;
+        w.vacc_m[j] = kFull;
+        const double d = fabs(S - expv[j]);
+        w.vact[j] = S;
+        dd[j] = d;
+        ww[j] = cert_window(S, T, mb, M, d);
     }
-    if (tid == 0) w.vcnt[g] = 0;
-    __threadfence();
     __syncthreads();
-    if (tid == 0) sel.flag = (atomicAdd(&w.vcnt[groups], 1) == groups - 1);
-    __syncthreads();
-    if (!sel.flag) return;
-    __threadfence();
 
-    // Last group: the reference's detection (k_detect_row) on exact values.
-    const int ec = final_select(
-        N, tau, expv, w.vact, w.vd, w.vw, [&](int j) { return exact_chain(C + j, ldc, M); }, sel);
+    // The reference's detection (k_detect_row) on exact values.
+    const int ec = final_select<false>(
+        N, tau, expv, w.vact, dd, ww, [&](int j) { return exact_chain(C + j, ldc, M); }, sel);
     if (tid == 0) {
-        const double rd = (ec >= 0) ? (__ldcg(w.vact + ec) - expv[ec]) : 0.0;
+        const double rd = (ec >= 0) ? (w.vact[ec] - expv[ec]) : 0.0;
         w.rec[f].errcol = ec;
         w.rec[f].errrow = -1;
         w.rec[f].rowdiff = rd;
@@ -316,7 +317,7 @@ __global__ void __launch_bounds__(kThreads)
             L.errrow = -1;
             L.rowdiff = rd;
         }
-        w.vcnt[groups] = 0;
+        *w.vcnt = 0;
     }
 }
 
@@ -374,7 +375,7 @@ __global__ void __launch_bounds__(kThreads)
     if (!sel.flag) return;
     __threadfence();
 
-    const int er = final_select(
+    const int er = final_select<true>(
         M, tau, expc, w.lact, w.ld, w.lw, [&](int i) { return exact_chain(C + (long long)i * ldc, 1, N); }, sel);
     if (tid == 0) {
         *w.lcnt = 0;
@@ -633,16 +634,30 @@ void verify_geometry(int sms, int M, int N, int& groups, int& chunks, int& rows_
 
 // ------------------------------------------------------------ launchers ---
 
+// Large dynamic shared memory must be enabled once per device and kernel.
+int ensure_kernel_attrs(int device) {
+    static std::mutex mu;
+    static std::set<int> done;
+    std::lock_guard<std::mutex> lock(mu);
+    if (done.count(device)) return ABFT_OK;
+    cudaError_t e = cudaSuccess;
+    auto set = [&](const void* fn, int bytes) {
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    };
+    set((const void*)k_colchain<false, true>, kColSmem);
+    set((const void*)k_colchain<false, false>, kColSmem);
+    set((const void*)k_colchain<true, true>, kColSmem);
+    set((const void*)k_colchain<true, false>, kColSmem);
+    set((const void*)k_verify<true>, kVerifySmemMax);
+    set((const void*)k_verify<false>, kVerifySmemMax);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+    done.insert(device);
+    return ABFT_OK;
+}
+
 int launch_encode(abft_ws* ws, const float* dA, int64_t lda, const float* dB, int64_t ldb, cudaStream_t st,
                   int* launches) {
-    static bool attr_done = false;
-    if (!attr_done) {
-        cudaFuncSetAttribute(k_colchain<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kColSmem);
-        cudaFuncSetAttribute(k_colchain<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kColSmem);
-        cudaFuncSetAttribute(k_colchain<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kColSmem);
-        cudaFuncSetAttribute(k_colchain<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kColSmem);
-        attr_done = true;
-    }
+    if (int rc = ensure_kernel_attrs(ws->device)) return rc;
     const int M = ws->M_b, K = ws->K, N = ws->N_b, F = ws->F;
     int n = 0;
     // colSumA[K]: chains over the M rows of A.
@@ -686,18 +701,23 @@ int launch_verify(abft_ws* ws, const float* dC, int64_t ldc, int f, double tau, 
                   cudaStream_t st) {
     const int M = ws->M_b, N = ws->counts[f];
     const float* Cf = dC + ws->offsets[f];
+    if (int rc = ensure_kernel_attrs(ws->device)) return rc;
     int groups, chunks, rows_per;
     verify_geometry(ws->sms, M, N, groups, chunks, rows_per);
     const bool vec = aligned16(Cf) && (ldc % 4 == 0) && (N % 4 == 0);
     dim3 grid(groups, chunks);
     const double* expv = ws->d.expRow + ws->offsets[f];
     if (it >= ws->max_iters) it = -1;
+    const int reduce_bytes = kWarps * kGroupCols * 16;
+    const int dw_in_smem = (16LL * N <= kVerifySmemMax) ? 1 : 0;
+    const int smem = dw_in_smem ? std::max(reduce_bytes, 16 * N) : reduce_bytes;
+    const int total = groups * chunks;
     if (vec)
-        k_verify<true><<<grid, kThreads, 0, st>>>(Cf, ldc, M, N, rows_per, chunks, groups, ws->nfpad, expv, tau,
-                                                  injected, f, ws->F, it, ws->d);
+        k_verify<true><<<grid, kThreads, smem, st>>>(Cf, ldc, M, N, rows_per, total, dw_in_smem, expv, tau,
+                                                     injected, f, ws->F, it, ws->d);
     else
-        k_verify<false><<<grid, kThreads, 0, st>>>(Cf, ldc, M, N, rows_per, chunks, groups, ws->nfpad, expv, tau,
-                                                   injected, f, ws->F, it, ws->d);
+        k_verify<false><<<grid, kThreads, smem, st>>>(Cf, ldc, M, N, rows_per, total, dw_in_smem, expv, tau,
+                                                      injected, f, ws->F, it, ws->d);
     return check_launch("verify");
 }
 

@@ -246,6 +246,7 @@ def run_ours(args):
     t = abft.rank_tile(M, K, N, Pr, Pc, rank, args.frags)
     s = abft.OnlineSession(A, B, counts=t.counts, offsets=t.offsets, max_iters=args.iters)
     s.set_tau([tau] * t.F)
+    s.encode()  # first call loads the kernels
     encode_ms = s.encode()
     s.baseline(1)
     torch.cuda.synchronize(dev)

@@ -226,6 +226,47 @@ int abft_session_read_injections(abft_session* s, int it_count, int* inj4, float
 int abft_session_run_host(abft_session* s, const float* hA, const float* hB, float* hC,
                           const abft_online_args* args, abft_online_result* res, double* e2e_ms);
 
+/* ------------------------------------------------------------------------
+ * Metrics (metrics/metrics.cuh, core/common.cuh:86-106): the confusion
+ * matrix, derived rates, GFLOPS, overhead, the stdout report and the
+ * 41-column append-mode CSV, formatted exactly like the reference.
+ * ---------------------------------------------------------------------- */
+typedef struct abft_timing {
+    double min_ms, median_ms, mean_ms, max_ms;
+    int n_samples;
+} abft_timing;
+
+typedef struct abft_metrics {
+    char scheme[16];     /* "baseline", "online", "calibrate"   */
+    char inject[16];     /* "none", "add", "swifi"              */
+    char swifi_zone[16];
+    int baseline_only, calibrate;
+    int M, K, N, Pr, Pc, frags_per_rank, num_fragments_total, repeats;
+    double threshold_used;
+    abft_timing baseline, protected_;
+    int cm[4]; /* TP, TN, FP, FN */
+    int n_restored;
+    double calib_max_diff, calib_safety_factor, calib_suggested_tau;
+    /* filled by abft_metrics_finalize */
+    double overhead_pct, recall, precision, correction_precision_pct;
+    double baseline_gflops_min, baseline_gflops_median, baseline_gflops_mean, baseline_gflops_max;
+    double protected_gflops_min, protected_gflops_median, protected_gflops_mean, protected_gflops_max;
+} abft_metrics;
+
+/* stats_of, core/common.cuh:86-106 (median = sorted[n/2]). */
+int abft_stats_of(const double* samples, int n, abft_timing* out);
+/* finalize_metrics, metrics/metrics.cuh:132-149 (with compute_* :105-130). */
+int abft_metrics_finalize(abft_metrics* m);
+/* print_metrics, metrics/metrics.cuh:152-211, written into buf (NUL-terminated).
+ * Returns the full length; truncates to cap - 1 characters. */
+int abft_metrics_report(const abft_metrics* m, char* buf, size_t cap);
+/* log_metrics_csv, metrics/metrics.cuh:214-254: appends one row, writing the
+ * header first when the file does not exist. extra_header / extra_values
+ * (both or neither) append further comma-separated columns after the
+ * reference's 41. */
+int abft_metrics_csv_append(const abft_metrics* m, const char* path, const char* extra_header,
+                            const char* extra_values);
+
 #ifdef __cplusplus
 }
 #endif

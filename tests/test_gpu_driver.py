@@ -1,0 +1,67 @@
+"""abft_gemm (this project) against the reference binary rebuilt for sm_100a
+(oracle/_ref/abft_gemm_ref, single rank): same flags, same seeds, same cuBLAS
+build -> every non-timing CSV column (confusion matrix, restore count,
+threshold, geometry) must be identical."""
+import csv
+import os
+import subprocess
+
+import pytest
+
+import refharness
+from conftest import PKG_NAME, ROOT
+
+DRIVER = os.path.join(ROOT, PKG_NAME, "abft_gemm")
+TIMING_COLS = {"baseline_min_ms", "baseline_median_ms", "baseline_mean_ms", "baseline_max_ms",
+               "baseline_gflops_min", "baseline_gflops_median", "baseline_gflops_mean", "baseline_gflops_max",
+               "protected_min_ms", "protected_median_ms", "protected_mean_ms", "protected_max_ms",
+               "protected_gflops_min", "protected_gflops_median", "protected_gflops_mean", "protected_gflops_max",
+               "overhead_pct"}
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not os.path.exists(refharness.REF_DRIVER), reason="reference binary not built")]
+
+CASES = [
+    ["1024", "--inject", "add", "--threshold", "0.01024"],
+    ["1024", "--inject", "swifi", "--threshold", "0.01024"],
+    ["1024", "--inject", "swifi"],                                     # formula threshold
+    ["1024", "--inject", "none", "--threshold", "0.01024"],
+    ["1024", "--baseline"],
+    ["1100", "300", "1030", "--inject", "swifi", "--swifi-zone", "exponent", "--threshold", "0.003"],
+    ["2048", "--inject", "swifi", "--swifi-zone", "sig_high", "--threshold", "0.02", "--frags-per-rank", "8"],
+    ["1024", "--inject", "swifi", "--reseed-per-trial", "--threshold", "0.01024"],
+    ["4096", "1024", "2048", "--inject", "add", "--threshold", "0.04", "--frag-cap", "1000000"],
+]
+
+
+def run(binary, args, csv_path, env_extra=None):
+    env = dict(os.environ)
+    env.update(env_extra or {})
+    for k in ("RANK", "WORLD_SIZE", "LOCAL_RANK"):
+        env.pop(k, None)
+    r = subprocess.run([binary] + args + ["--csv", csv_path], capture_output=True, text=True, timeout=600, env=env)
+    assert r.returncode == 0, (binary, r.stdout[-2000:], r.stderr[-2000:])
+    with open(csv_path) as f:
+        rows = list(csv.DictReader(f))
+    assert len(rows) == 1
+    return rows[0], r.stdout
+
+
+@pytest.mark.parametrize("case", CASES, ids=[" ".join(c) for c in CASES])
+def test_driver_matches_reference_binary(case, tmp_path):
+    common = ["--repeats", "10", "--samples", "2", "--warmups", "1"]
+    ours, out_ours = run(DRIVER, case + common, str(tmp_path / "ours.csv"))
+    ref, out_ref = run(refharness.REF_DRIVER, case + common, str(tmp_path / "ref.csv"))
+    assert list(ours.keys()) == list(ref.keys())
+    for k in ref:
+        if k not in TIMING_COLS:
+            assert ours[k] == ref[k], (k, ours[k], ref[k])
+    assert "TP / TN / FP / FN" in out_ours
+
+
+def test_driver_rejects_bad_flags(tmp_path):
+    r = subprocess.run([DRIVER, "64", "--inject", "bogus"], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 2 and "inject" in r.stderr
+    r = subprocess.run([DRIVER, "64", "--grid", "2", "2"], capture_output=True, text=True, timeout=60,
+                       cwd=str(tmp_path))
+    assert r.returncode == 1 and "does not match" in r.stderr
