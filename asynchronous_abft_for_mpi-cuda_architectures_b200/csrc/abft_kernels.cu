@@ -40,9 +40,14 @@ namespace {
 
 constexpr unsigned kFull = 0xffffffffu;
 constexpr int kListCap = 256;
-constexpr int kBatch = 16;  // rows in flight per warp in the verify body
+constexpr int kBatch = 8;   // rows in flight per warp in the verify body
 
 // ------------------------------------------------------------- helpers ----
+
+// Release/acquire fence at device scope: orders this thread's earlier global
+// writes (and atomics) before its later ones as seen by other CTAs; used around
+// the arrival counters of the last-CTA-finalises pattern.
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;\n" ::: "memory"); }
 
 // Window w >= 0 with |d_reference - d| <= w for a sum S of n float terms with
 // float |x|-sum T and smallest (|x| bits - 1) mbm1; w == 0 means S (and so d)
@@ -55,7 +60,9 @@ __device__ __forceinline__ double cert_window(double S, float T, uint32_t mbm1, 
     int e = (int)(nz >> 23);
     if (e < 1) e = 1;
     const double tb = (double)T * (1.0 + 4.0 * (double)n * 0x1p-24);  // upper bound of sum |x|
-    if (tb <= ldexp(1.0, e - 97)) return 0.0;                          // 2^(p+53), p = e - 150
+    // 2^(p+53) with p = e - 150, built from its bits (e - 97 >= -96: always a normal double)
+    const double limit = __longlong_as_double((long long)(e - 97 + 1023) << 52);
+    if (tb <= limit) return 0.0;
     const double E = 2.0 * (double)n * 0x1p-53 * tb * (1.0 + 0x1p-30);
     const double w = E * (1.0 + 0x1p-40) + d * 0x1p-51 + 0x1p-1000;
     return (w > 0.0) ? w : INFINITY;
@@ -117,51 +124,64 @@ template <bool CG, class Exact>
 __device__ int final_select(int n, double tau, const double* __restrict__ expv, double* act, double* dd, double* ww,
                             Exact exact, SelectSmem& sm) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    // Pass 1: largest certified candidate; is there any candidate at all, any uncertified one?
     double bc = -INFINITY;
+    int anyc = 0, anyu = 0;
 #pragma unroll 4
     for (int j = tid; j < n; j += kThreads) {
         const double wv = ld_sel<CG>(ww + j), dv = ld_sel<CG>(dd + j);
         if (wv == 0.0 && dv > tau && dv > bc) bc = dv;
+        if (dv + wv > tau) {
+            anyc = 1;
+            if (wv != 0.0) anyu = 1;
+        }
     }
-    sm.d[tid] = bc;
-    __syncthreads();
-    for (int s = kThreads / 2; s > 0; s >>= 1) {
-        if (tid < s && sm.d[tid + s] > sm.d[tid]) sm.d[tid] = sm.d[tid + s];
-        __syncthreads();
-    }
-    const double best_cert = sm.d[0];
-    __syncthreads();
+    if (!__syncthreads_or(anyc)) return -1;  // every |actual - expected| <= tau
+    anyu = __syncthreads_or(anyu);
 
-    for (;;) {
-        if (tid == 0) sm.cnt = 0;
+    if (anyu) {
+        // the maximum is order independent: warp shuffles, then across warps
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) bc = fmax(bc, __shfl_xor_sync(kFull, bc, o));
+        if (lane == 0) sm.d[warp] = bc;
         __syncthreads();
+        double best_cert = sm.d[0];
+        for (int k = 1; k < kWarps; ++k) best_cert = fmax(best_cert, sm.d[k]);
+        __syncthreads();
+        for (;;) {
+            if (tid == 0) sm.cnt = 0;
+            __syncthreads();
 #pragma unroll 4
-        for (int j = tid; j < n; j += kThreads) {
-            const double wv = ld_sel<CG>(ww + j);
-            if (wv != 0.0) {
-                const double hi = ld_sel<CG>(dd + j) + wv;
-                if (hi > tau && hi >= best_cert) {
-                    const int k = atomicAdd(&sm.cnt, 1);
-                    if (k < kListCap) sm.list[k] = j;
+            for (int j = tid; j < n; j += kThreads) {
+                const double wv = ld_sel<CG>(ww + j);
+                if (wv != 0.0) {
+                    const double hi = ld_sel<CG>(dd + j) + wv;
+                    if (hi > tau && hi >= best_cert) {
+                        const int k = atomicAdd(&sm.cnt, 1);
+                        if (k < kListCap) sm.list[k] = j;
+                    }
                 }
             }
-        }
-        __syncthreads();
-        const int cnt = sm.cnt;
-        const int todo = min(cnt, kListCap);
-        for (int k = warp; k < todo; k += kWarps) {
-            const int j = sm.list[k];
-            const double S = exact(j);
-            if (lane == 0) {
-                act[j] = S;
-                dd[j] = fabs(S - expv[j]);
-                ww[j] = 0.0;
+            __syncthreads();
+            const int cnt = sm.cnt;
+            const int todo = min(cnt, kListCap);
+            for (int k = warp; k < todo; k += kWarps) {
+                const int j = sm.list[k];
+                const double S = exact(j);
+                if (lane == 0) {
+                    act[j] = S;
+                    dd[j] = fabs(S - expv[j]);
+                    ww[j] = 0.0;
+                }
             }
+            __syncthreads();
+            if (cnt <= kListCap) break;
         }
-        __syncthreads();
-        if (cnt <= kListCap) break;
     }
 
+    // Pass 3: the reference's 256-slot strided scan and shared-memory tree
+    // (strictly larger right operand wins); the last five tree levels run as
+    // warp shuffles inside warp 0, pairing the same slots.
     double best = 0.0;
     int bj = -1;
 #pragma unroll 4
@@ -177,13 +197,28 @@ __device__ int final_select(int n, double tau, const double* __restrict__ expv, 
     sm.d[tid] = best;
     sm.j[tid] = bj;
     __syncthreads();
-    for (int s = kThreads / 2; s > 0; s >>= 1) {
+    for (int s = kThreads / 2; s >= 32; s >>= 1) {
         if (tid < s && sm.d[tid + s] > sm.d[tid]) {
             sm.d[tid] = sm.d[tid + s];
             sm.j[tid] = sm.j[tid + s];
         }
         __syncthreads();
     }
+    if (warp == 0) {
+        double v = sm.d[lane];
+        int vj = sm.j[lane];
+#pragma unroll
+        for (int s = 16; s > 0; s >>= 1) {
+            const double ov = __shfl_down_sync(kFull, v, s);
+            const int oj = __shfl_down_sync(kFull, vj, s);
+            if (lane < s && ov > v) {
+                v = ov;
+                vj = oj;
+            }
+        }
+        if (lane == 0) sm.j[0] = vj;
+    }
+    __syncthreads();
     const int w = sm.j[0];
     __syncthreads();
     return w;
@@ -200,7 +235,7 @@ __device__ int final_select(int n, double tau, const double* __restrict__ expv, 
 // runs the reference's arg-max. Shared memory: 16 KB for the CTA reduction,
 // reused by the last CTA for the d / w arrays when 16*N bytes fit.
 template <bool VEC>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 4)
     k_verify(const float* __restrict__ C, long long ldc, int M, int N, int rows_per, int total_ctas, int dw_in_smem,
              const double* __restrict__ expv, double tau, int injected, int f, int F, int it, WsDev w) {
     extern __shared__ __align__(16) unsigned char dsm[];
@@ -275,28 +310,44 @@ __global__ void __launch_bounds__(kThreads)
             atomicMin(w.vacc_m + col, mb);
         }
     }
-    __threadfence();
+    fence_acq_rel_gpu();
     __syncthreads();
     if (tid == 0) sel.flag = (atomicAdd(w.vcnt, 1) == total_ctas - 1);
     __syncthreads();
     if (!sel.flag) return;
-    __threadfence();
+    fence_acq_rel_gpu();
 
     // Last CTA: certify every column, reset the accumulators for the next launch.
+    // Loads of a batch are issued before any store so that they overlap.
     double* dd = dw_in_smem ? reinterpret_cast<double*>(dsm) : w.vd;
     double* ww = dw_in_smem ? reinterpret_cast<double*>(dsm) + N : w.vw;
-#pragma unroll 4
-    for (int j = tid; j < N; j += kThreads) {
-        const double S = __ldcg(w.vacc_s + j);
-        const float T = __ldcg(w.vacc_t + j);
-        const uint32_t mb = __ldcg(w.vacc_m + j);
-        w.vacc_s[j] = 0.0;
-        w.vacc_t[j] = 0.f;
-        w.vacc_m[j] = kFull;
-        const double d = fabs(S - expv[j]);
-        w.vact[j] = S;
-        dd[j] = d;
-        ww[j] = cert_window(S, T, mb, M, d);
+    for (int base = 0; base < N; base += 4 * kThreads) {
+        double S[4], E[4];
+        float T[4];
+        uint32_t MB[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int j = base + u * kThreads + tid;
+            if (j < N) {
+                S[u] = __ldcg(w.vacc_s + j);
+                T[u] = __ldcg(w.vacc_t + j);
+                MB[u] = __ldcg(w.vacc_m + j);
+                E[u] = expv[j];
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int j = base + u * kThreads + tid;
+            if (j < N) {
+                w.vacc_s[j] = 0.0;
+                w.vacc_t[j] = 0.f;
+                w.vacc_m[j] = kFull;
+                const double d = fabs(S[u] - E[u]);
+                w.vact[j] = S[u];
+                dd[j] = d;
+                ww[j] = cert_window(S[u], T[u], MB[u], M, d);
+            }
+        }
     }
     __syncthreads();
 
@@ -368,12 +419,12 @@ __global__ void __launch_bounds__(kThreads)
             w.lw[r] = cert_window(s, t, m, N, d);
         }
     }
-    __threadfence();
+    fence_acq_rel_gpu();
     __syncthreads();
     if (tid == 0) sel.flag = (atomicAdd(w.lcnt, 1) == nblocks - 1);
     __syncthreads();
     if (!sel.flag) return;
-    __threadfence();
+    fence_acq_rel_gpu();
 
     const int er = final_select<true>(
         M, tau, expc, w.lact, w.ld, w.lw, [&](int i) { return exact_chain(C + (long long)i * ldc, 1, N); }, sel);
@@ -621,7 +672,7 @@ int check_launch(const char* what) {
 // Verify geometry: column groups x row chunks, about two CTAs per SM.
 void verify_geometry(int sms, int M, int N, int& groups, int& chunks, int& rows_per) {
     groups = (N + kGroupCols - 1) / kGroupCols;
-    int target = 2 * sms;
+    int target = 4 * sms;
     chunks = (target + groups - 1) / groups;
     if (chunks < 1) chunks = 1;
     if (chunks > kMaxChunks) chunks = kMaxChunks;
