@@ -273,6 +273,16 @@ int abft_verify(abft_ws* ws, const float* dC, int64_t ldc, int f, double tau, in
     return launch_verify(ws, dC, ldc, f, tau, injected ? 1 : 0, it, (cudaStream_t)stream);
 }
 
+int abft_verify_noalloc(const float* dC_frag, int64_t ldc, int M, int N, const double* dExpRow, double tau,
+                        int injected, int* dErrCol, double* dRowDiff, int* dCM, void* stream) {
+    if (!dC_frag || !dExpRow || !dErrCol || !dRowDiff || !dCM || M < 1 || N < 1 || ldc < N) {
+        set_error("abft_verify_noalloc: bad argument (pointers, M >= 1, N >= 1, ldc >= N)");
+        return ABFT_ERR_ARG;
+    }
+    return launch_verify_static(dC_frag, ldc, M, N, dExpRow, tau, injected ? 1 : 0, dErrCol, dRowDiff, dCM,
+                                (cudaStream_t)stream);
+}
+
 int abft_localize_correct(abft_ws* ws, float* dC, int64_t ldc, int f, double tau, int injected, const float* dGolden,
                           int64_t ldg, int it, int correct_mode, void* stream) {
     if (!ws || !dC || f < 0 || f >= ws->F || ldc < ws->N_b || (dGolden && ldg < ws->N_b) ||

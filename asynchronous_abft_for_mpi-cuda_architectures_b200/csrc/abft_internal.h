@@ -112,5 +112,7 @@ int launch_drain(abft_ws* ws, float* dC0, float* dC1, int64_t ldc, const float* 
                  cudaStream_t st);
 int launch_inject(float* dC, int64_t ldc, int row, int col, int mode, float delta, int bit, InjectLog* log,
                   int frag, cudaStream_t st);
+int launch_verify_static(const float* Cf, int64_t ldc, int M, int N, const double* expv, double tau, int injected,
+                         int* errcol, double* rowdiff, int* cm, cudaStream_t st);
 
 }  // namespace abft

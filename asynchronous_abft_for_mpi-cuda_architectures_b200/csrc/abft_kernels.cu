@@ -31,6 +31,7 @@
 #include <algorithm>
 #include <mutex>
 #include <set>
+#include <string>
 
 #include "abft_b200.h"
 #include "abft_internal.h"
@@ -811,6 +812,119 @@ int launch_inject(float* dC, int64_t ldc, int row, int col, int mode, float delt
                   int frag, cudaStream_t st) {
     k_inject<<<1, 1, 0, st>>>(dC, ldc, row, col, mode, delta, bit, log, frag);
     return check_launch("inject");
+}
+
+}  // namespace abft
+
+// ------------------------------------------------ verify without allocation --
+//
+// abft_verify_noalloc runs the fused verify kernel above on scratch that lives
+// in a static device array of this library instead of a workspace, for callers
+// that may not allocate device memory (see include/abft_b200.h). The array is
+// at most kStaticMaxCols columns wide:
+//   [0, 32 KiB)        per-column double sums         (double[4096])
+//   [32 KiB, 48 KiB)   per-column float |x| sums      (float[4096])
+//   [48 KiB, 64 KiB)   per-column smallest |x| bits-1 (uint32[4096], starts at 0xffffffff)
+//   [64 KiB, 96 KiB)   per-column final sums          (double[4096])
+//   then one arrival counter, one decision record and one counter block,
+//   256 bytes each.
+// Every call on a device shares the array. The kernel's last CTA puts the
+// accumulators and the arrival counter back to their start values, and the
+// copy-out kernel zeroes the counter block, so each call starts clean; two
+// calls whose kernels overlap on the GPU race on the array.
+namespace abft {
+namespace {
+
+constexpr int kStaticMaxCols = 4096;
+constexpr size_t kStaticColBytes = 96 * 1024;
+constexpr size_t kStaticScratchBytes = kStaticColBytes + 3 * 256;
+static __device__ __align__(256) unsigned char g_verify_scratch[kStaticScratchBytes];
+
+struct StaticScratchState {
+    bool ready = false;
+    unsigned char* base = nullptr;  // device address of g_verify_scratch on this device
+    int sms = 0;
+};
+constexpr int kMaxDevices = 64;
+std::mutex g_static_mu;
+StaticScratchState g_static[kMaxDevices];
+
+// One-time set-up per device, with that device current: resolve the device
+// address of the static array (host code may not use the symbol itself) and
+// bring it to its start values on the caller's stream.
+int static_scratch(int device, cudaStream_t st, StaticScratchState* out) {
+    std::lock_guard<std::mutex> lock(g_static_mu);
+    if (device < 0 || device >= kMaxDevices) {
+        set_error("abft_verify_noalloc: device index out of range");
+        return ABFT_ERR_ARG;
+    }
+    StaticScratchState& s = g_static[device];
+    if (!s.ready) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_verify_scratch);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(verify scratch)");
+        e = cudaMemsetAsync(p, 0, kStaticScratchBytes, st);
+        if (e == cudaSuccess) e = cudaMemsetAsync(static_cast<unsigned char*>(p) + 48 * 1024, 0xff, 16 * 1024, st);
+        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&s.sms, cudaDevAttrMultiProcessorCount, device);
+        if (e != cudaSuccess) return cuda_fail(e, "verify scratch set-up");
+        s.base = static_cast<unsigned char*>(p);
+        s.ready = true;
+    }
+    *out = s;
+    return ABFT_OK;
+}
+
+__global__ void k_static_copyout(const FragRecord* rec, Counters* ctr, int* errcol, double* rowdiff, int* cm) {
+    if (threadIdx.x == 0) {
+        *errcol = rec->errcol;
+        *rowdiff = rec->rowdiff;
+        for (int i = 0; i < 4; ++i) {
+            const int v = ctr->cm[i];
+            if (v != 0) atomicAdd(cm + i, v);
+            ctr->cm[i] = 0;
+        }
+    }
+}
+
+}  // namespace
+
+int launch_verify_static(const float* Cf, int64_t ldc, int M, int N, const double* expv, double tau, int injected,
+                         int* errcol, double* rowdiff, int* cm, cudaStream_t st) {
+    if (N > kStaticMaxCols) {
+        set_error("abft_verify_noalloc: fragment has " + std::to_string(N) + " columns; the static scratch holds " +
+                  std::to_string(kStaticMaxCols));
+        return ABFT_ERR_ARG;
+    }
+    int device = 0;
+    cudaError_t e = cudaGetDevice(&device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    StaticScratchState s;
+    if (int rc = static_scratch(device, st, &s)) return rc;
+    if (int rc = ensure_kernel_attrs(device)) return rc;
+    WsDev w{};
+    w.vacc_s = reinterpret_cast<double*>(s.base);
+    w.vacc_t = reinterpret_cast<float*>(s.base + 32 * 1024);
+    w.vacc_m = reinterpret_cast<uint32_t*>(s.base + 48 * 1024);
+    w.vact = reinterpret_cast<double*>(s.base + 64 * 1024);
+    w.vcnt = reinterpret_cast<int*>(s.base + kStaticColBytes);
+    w.rec = reinterpret_cast<FragRecord*>(s.base + kStaticColBytes + 256);
+    w.ctr = reinterpret_cast<Counters*>(s.base + kStaticColBytes + 512);
+    int groups, chunks, rows_per;
+    verify_geometry(s.sms, M, N, groups, chunks, rows_per);
+    const bool vec = aligned16(Cf) && (ldc % 4 == 0) && (N % 4 == 0);
+    const int reduce_bytes = kWarps * kGroupCols * 16;
+    const int smem = std::max(reduce_bytes, 16 * N);  // d / w always fit: N <= kStaticMaxCols
+    dim3 grid(groups, chunks);
+    const int total = groups * chunks;
+    if (vec)
+        k_verify<true><<<grid, kThreads, smem, st>>>(Cf, ldc, M, N, rows_per, total, 1, expv, tau, injected, 0, 1,
+                                                     -1, w);
+    else
+        k_verify<false><<<grid, kThreads, smem, st>>>(Cf, ldc, M, N, rows_per, total, 1, expv, tau, injected, 0, 1,
+                                                      -1, w);
+    if (int rc = check_launch("verify (static scratch)")) return rc;
+    k_static_copyout<<<1, 32, 0, st>>>(w.rec, w.ctr, errcol, rowdiff, cm);
+    return check_launch("verify copy-out");
 }
 
 }  // namespace abft

@@ -128,6 +128,26 @@ int abft_encode(abft_ws* ws, const float* dA, int64_t lda, const float* dB, int6
  * rank tile's base pointer. `it` indexes the decision log (-1 = no log). */
 int abft_verify(abft_ws* ws, const float* dC, int64_t ldc, int f, double tau, int injected, int it, void* stream);
 
+/* Verify one fragment without allocating anything. No counterpart in the
+ * reference: it exists for callers that must not allocate device memory while
+ * they run - a fault-tolerance hook called from inside another library's hot
+ * loop, or a service whose device memory is fixed at start-up - because
+ * cudaMalloc/cudaFree can synchronise the whole device and can fail under
+ * memory pressure. Same computation and decision as abft_verify, but the
+ * caller passes everything: the fragment dC_frag (M x N, leading dimension
+ * ldc), its expected row dExpRow[N] (e.g. from abft_encode), and the outputs
+ * dErrCol (int), dRowDiff (double) and dCM (int[4], TP TN FP FN, incremented).
+ * Scratch is a static device array inside this library, held by every GPU that
+ * loads it until the process exits, limited to N <= 4096 columns (larger N
+ * returns ABFT_ERR_ARG). The first call on a device sets that array up (it
+ * looks up the array's device address and clears it on `stream`); make that
+ * first call before any stream capture. All calls on a device share the
+ * array: calls whose work overlaps on the GPU race; calls ordered one after
+ * another (same stream, or synchronised) are safe. No cudaMalloc, cudaFree or
+ * allocating library routine is called. */
+int abft_verify_noalloc(const float* dC_frag, int64_t ldc, int M, int N, const double* dExpRow, double tau,
+                        int injected, int* dErrCol, double* dRowDiff, int* dCM, void* stream);
+
 /* Localise and correct fragment f, gated on the device by the verify result:
  * replaces launch_localize_correct (kernels/abft_stepwise.cuh:218-239).
  * dGolden (may be NULL) is the fault-free tile with leading dimension ldg,
