@@ -73,15 +73,16 @@ def peak_hbm():
 
 
 def verify_traffic_per_launch(tile, frags):
-    """DRAM bytes per verify launch from the committed ncu summary, if one matches this workload."""
-    path = os.path.join(ROOT, "profiles", "verify_traffic.json")
+    """DRAM bytes per verify launch from the committed ncu summary of this fragment shape, if any."""
+    path = os.path.join(ROOT, "profiles", f"verify_{tile}x{tile // frags}.md")
     try:
         with open(path) as f:
-            d = json.load(f)
-        key = f"{tile}x{tile // frags}"
-        return d.get(key)
-    except Exception:
-        return None
+            for line in f:
+                if line.startswith("traffic_bytes_per_launch:"):
+                    return float(line.split(":")[1])
+    except OSError:
+        pass
+    return None
 
 
 class ClockSampler:
