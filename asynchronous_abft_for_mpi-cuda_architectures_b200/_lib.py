@@ -49,7 +49,7 @@ class OnlineArgs(ctypes.Structure):
         ("mode", ctypes.c_int), ("zone_lo", ctypes.c_int), ("zone_hi", ctypes.c_int),
         ("add_delta", ctypes.c_float), ("base_seed", ctypes.c_uint64), ("rank", ctypes.c_int),
         ("repeats", ctypes.c_int), ("correct_mode", ctypes.c_int), ("log", ctypes.c_int),
-        ("profile", ctypes.c_int),
+        ("profile", ctypes.c_int), ("graph", ctypes.c_int),
     ]
 
 
@@ -117,6 +117,7 @@ SIGNATURES = {
     "abft_ws_read_checksums": (_I, [_P, _DP, _DP, _DP, _DP]),
     "abft_encode": (_I, [_P, _P, _I64, _P, _I64, _P]),
     "abft_verify": (_I, [_P, _P, _I64, _I, _D, _I, _I, _P]),
+    "abft_calibrate": (_I, [_P, _P, _I64, _I, _P, _P]),
     "abft_verify_noalloc": (_I, [_P, _I64, _I, _I, _P, _D, _I, _P, _P, _P, _P]),
     "abft_localize_correct": (_I, [_P, _P, _I64, _I, _D, _I, _P, _I64, _I, _I, _P]),
     "abft_drain": (_I, [_P, _P, _P, _I64, _P, _I64, _I, _P]),
@@ -129,7 +130,7 @@ SIGNATURES = {
     "abft_session_set_tau": (_I, [_P, _DP]),
     "abft_session_set_golden": (_I, [_P, _P, _I64]),
     "abft_session_encode": (_I, [_P, _DP]),
-    "abft_session_baseline": (_I, [_P, _I, _DP, _DP]),
+    "abft_session_baseline": (_I, [_P, _I, _I, _DP, _DP]),
     "abft_session_online": (_I, [_P, ctypes.POINTER(OnlineArgs), ctypes.POINTER(OnlineResult)]),
     "abft_session_read_injections": (_I, [_P, _I, _IP, ctypes.POINTER(ctypes.c_float)]),
     "abft_session_run_host": (_I, [_P, _P, _P, _P, ctypes.POINTER(OnlineArgs), ctypes.POINTER(OnlineResult),

@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstdio>
 #include <cstring>
 #include <new>
@@ -55,6 +56,7 @@ WsLayout ws_layout(int M_b, int N_b, int K, int F, int nfmax, int max_iters) {
     L.dlog = take(sizeof(DecisionLog) * (size_t)std::max(max_iters, 1) * F);
     L.ilog = take(sizeof(InjectLog) * (size_t)std::max(max_iters, 1));
     L.pend = take(sizeof(PendingFix) * (size_t)std::max(max_iters, 1) * F);
+    L.plan = take(sizeof(InjectPlan) * (size_t)std::max(max_iters, 1));
     L.total = o;
     return L;
 }
@@ -175,6 +177,7 @@ int abft_ws_create(int M_b, int N_b, int K, int F, const int* counts, const int*
     d.dlog = reinterpret_cast<DecisionLog*>(b + L.dlog);
     d.ilog = reinterpret_cast<InjectLog*>(b + L.ilog);
     d.pend = reinterpret_cast<PendingFix*>(b + L.pend);
+    d.plan = reinterpret_cast<InjectPlan*>(b + L.plan);
     *out = ws;
     return ABFT_OK;
 }
@@ -271,6 +274,14 @@ int abft_verify(abft_ws* ws, const float* dC, int64_t ldc, int f, double tau, in
         return ABFT_ERR_ARG;
     }
     return launch_verify(ws, dC, ldc, f, tau, injected ? 1 : 0, it, (cudaStream_t)stream);
+}
+
+int abft_calibrate(abft_ws* ws, const float* dC, int64_t ldc, int f, double* dDiff, void* stream) {
+    if (!ws || !dC || !dDiff || f < 0 || f >= ws->F || ldc < ws->N_b) {
+        set_error("abft_calibrate: bad argument (fragment index, pointers or ldc < N_b)");
+        return ABFT_ERR_ARG;
+    }
+    return launch_verify(ws, dC, ldc, f, INFINITY, 0, -1, (cudaStream_t)stream, -1, 0.f, 0, dDiff);
 }
 
 int abft_verify_noalloc(const float* dC_frag, int64_t ldc, int M, int N, const double* dExpRow, double tau,

@@ -201,3 +201,30 @@ std::string comm_recv(Comm& c, void* dev, size_t count, int peer) {
     if (r != ncclSuccess) return nccl_msg(r, "recv");
     return sync(c);
 }
+
+std::string comm_send_host(Comm& c, const void* host, size_t bytes, int peer) {
+    if (bytes == 0) return "";
+    void* dev = nullptr;
+    cudaError_t e = cudaMalloc(&dev, bytes);
+    if (e == cudaSuccess) e = cudaMemcpy(dev, host, bytes, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return std::string("staging: ") + cudaGetErrorString(e);
+    ncclResult_t r = ncclSend(dev, bytes, ncclChar, peer, c.world_comm, c.stream);
+    std::string err = (r != ncclSuccess) ? nccl_msg(r, "send") : sync(c);
+    cudaFree(dev);
+    return err;
+}
+
+std::string comm_recv_host(Comm& c, void* host, size_t bytes, int peer) {
+    if (bytes == 0) return "";
+    void* dev = nullptr;
+    cudaError_t e = cudaMalloc(&dev, bytes);
+    if (e != cudaSuccess) return std::string("staging: ") + cudaGetErrorString(e);
+    ncclResult_t r = ncclRecv(dev, bytes, ncclChar, peer, c.world_comm, c.stream);
+    std::string err = (r != ncclSuccess) ? nccl_msg(r, "recv") : sync(c);
+    if (err.empty()) {
+        e = cudaMemcpy(host, dev, bytes, cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) err = std::string("staging: ") + cudaGetErrorString(e);
+    }
+    cudaFree(dev);
+    return err;
+}

@@ -44,3 +44,7 @@ std::string comm_bcast(Comm& c, ncclComm_t comm, void* dev, size_t count_floats,
 // Point-to-point float transfer on the world communicator.
 std::string comm_send(Comm& c, const void* dev, size_t count_floats, int peer);
 std::string comm_recv(Comm& c, void* dev, size_t count_floats, int peer);
+// Byte transfers of HOST buffers, staged through device memory (end-of-run
+// payloads such as the calibration diffs).
+std::string comm_send_host(Comm& c, const void* host, size_t bytes, int peer);
+std::string comm_recv_host(Comm& c, void* host, size_t bytes, int peer);

@@ -8,8 +8,11 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstdio>
+#include <fstream>
+#include <iomanip>
 #include <cstdlib>
 #include <cstring>
 #include <iostream>
@@ -46,6 +49,7 @@ struct Config {
     int verify_priority = -1;
     double relative_threshold = -1.0;  // tau = r * K * max|A| * max|B|
     bool csv_extra = false;
+    bool graph = false;
 };
 
 void print_help() {
@@ -68,7 +72,9 @@ void print_help() {
         "  --reseed-per-trial             fresh A, B for every trial\n"
         "  --seed-a S, --seed-b S         input seeds (default 123456, 987654)\n"
         "  --csv PATH                     metrics CSV (default abft_metrics.csv)\n"
-        "  --calibrate, --calibration-safety F, --calib-diffs PATH   (not available in this build)\n"
+        "  --calibrate                    report max |actual-expected| and a suggested threshold\n"
+        "  --calibration-safety F         multiplier on the observed max (default 10)\n"
+        "  --calib-diffs PATH             every observed |actual-expected| (default abft_calibration_diffs.csv)\n"
         "Extensions:\n"
         "  --dist {uniform|normal}        input distribution (default uniform[-1,1])\n"
         "  --add-delta D                  additive fault size (default 1e6)\n"
@@ -76,6 +82,7 @@ void print_help() {
         "  --correct {inloop|drain}       correct inside the loop or after it\n"
         "  --verify-priority {low|default|high}\n"
         "  --csv-extra                    append encode/verify columns to the CSV\n"
+        "  --graph                        replay each trial's loop as a CUDA graph\n"
         "  --help                         this message\n";
 }
 
@@ -117,6 +124,7 @@ bool parse(int argc, char** argv, Config& c, std::string& err) {
             std::string m = argv[++i];
             c.verify_priority = (m == "high") ? 1 : (m == "default" ? 0 : -1);
         } else if (a == "--csv-extra") c.csv_extra = true;
+        else if (a == "--graph") c.graph = true;
         else if (a == "--help" || a == "-h") { print_help(); std::exit(0); }
         else if (!a.empty() && a[0] != '-') pos.push_back(std::atoi(argv[i]));
         else { err = "unknown or incomplete flag " + a; return false; }
@@ -170,7 +178,6 @@ int main(int argc, char** argv) {
     Config cfg;
     std::string perr;
     if (!parse(argc, argv, cfg, perr)) return die(perr, 2);
-    if (cfg.calibrate) return die("--calibrate is not available in this build", 2);
 
     const RankEnv env = rank_env_from_environment();
     const int world_rank = env.rank, world_size = env.world;
@@ -203,7 +210,7 @@ int main(int argc, char** argv) {
     std::vector<int> fc(F), fo(F);
     ABFT_TRY(abft_split_dim(N_b, F, fc.data(), fo.data()));
 
-    const std::string mode_label = cfg.baseline_only ? "baseline" : "online";
+    const std::string mode_label = cfg.calibrate ? "calibrate" : (cfg.baseline_only ? "baseline" : "online");
     const int NUM_TRIALS = cfg.num_samples > 0 ? cfg.num_samples : 5;
     if (world_rank == 0) {
         std::cout << "=== ABFT GEMM (cuBLAS, online pipelined) ===\n"
@@ -311,7 +318,34 @@ int main(int argc, char** argv) {
     int cm_local[4] = {0, 0, 0, 0};
     int restored_local = 0;
     bool golden_set = false;
-    for (int t = 0; t < TOTAL; ++t) {
+    double calib_max_local = 0.0;
+    std::vector<double> calib_diffs_local;
+    if (cfg.calibrate) {
+        // pass_calibrate (pipeline/passes.cuh:38-86) `repeats` times, each one
+        // timed sample: fragment SGEMMs, encode, every column's
+        // |actual - expected|, read back to the host.
+        double* dDiff = nullptr;
+        CUDA_TRY(cudaMalloc(&dDiff, sizeof(double) * N_b));
+        std::vector<double> hd(N_b);
+        abft_ws* ws = abft_session_ws(sess);
+        for (int it = 0; it < cfg.repeats; ++it) {
+            COMM_TRY(comm_barrier(comm));
+            const auto t0 = std::chrono::high_resolution_clock::now();
+            double dms = 0, hms = 0, enc = 0;
+            ABFT_TRY(abft_session_baseline(sess, 1, 0, &dms, &hms));
+            ABFT_TRY(abft_session_encode(sess, &enc));
+            for (int f = 0; f < F; ++f) ABFT_TRY(abft_calibrate(ws, dC0, N_b, f, dDiff + fo[f], nullptr));
+            CUDA_TRY(cudaMemcpy(hd.data(), dDiff, sizeof(double) * N_b, cudaMemcpyDeviceToHost));
+            for (int j = 0; j < N_b; ++j) {
+                calib_diffs_local.push_back(hd[j]);
+                if (hd[j] > calib_max_local) calib_max_local = hd[j];
+            }
+            const auto t1 = std::chrono::high_resolution_clock::now();
+            prot_samples.push_back(std::chrono::duration<double, std::milli>(t1 - t0).count());
+        }
+        cudaFree(dDiff);
+    }
+    for (int t = 0; t < (cfg.calibrate ? 0 : TOTAL); ++t) {
         const bool record = (t >= NUM_WARMUP);
         if (cfg.reseed_per_trial) {
             if (int r = regen(cfg.seed_a + (unsigned long long)t * 1000003ull, cfg.seed_b + (unsigned long long)t * 1000033ull))
@@ -319,7 +353,7 @@ int main(int argc, char** argv) {
         }
         COMM_TRY(comm_barrier(comm));
         double bdev = 0, bhost = 0;
-        ABFT_TRY(abft_session_baseline(sess, cfg.repeats, &bdev, &bhost));
+        ABFT_TRY(abft_session_baseline(sess, cfg.repeats, cfg.graph ? 1 : 0, &bdev, &bhost));
         if (record) base_samples.push_back(bhost / cfg.repeats);
         // Golden capture (main.cu:217-226). The reference uploads it to the
         // device only once (pipeline/passes.cuh:110-116), so only the first
@@ -348,6 +382,7 @@ int main(int argc, char** argv) {
         a.repeats = cfg.repeats;
         a.correct_mode = cfg.correct_mode;
         a.log = 0;
+        a.graph = cfg.graph ? 1 : 0;
         abft_online_result res{};
         COMM_TRY(comm_barrier(comm));
         ABFT_TRY(abft_session_online(sess, &a, &res));
@@ -357,7 +392,7 @@ int main(int argc, char** argv) {
             restored_local += res.n_restored;
         }
     }
-    if (world_rank == 0 && !cfg.baseline_only)
+    if (world_rank == 0 && !cfg.baseline_only && !cfg.calibrate)
         std::cout << "[Rank 0] " << NUM_TRIALS << " timed trials x " << cfg.repeats << " iters/trial"
                   << (cfg.reseed_per_trial ? "  (fresh A,B per trial)" : "") << "\n";
 
@@ -366,8 +401,35 @@ int main(int argc, char** argv) {
     ABFT_TRY(abft_stats_of(prot_samples.data(), (int)prot_samples.size(), &pl));
     int agg[5] = {cm_local[0], cm_local[1], cm_local[2], cm_local[3], restored_local};
     COMM_TRY(comm_allreduce_int_sum(comm, agg, 5));
-    double tm[8] = {bl.min_ms, bl.median_ms, bl.mean_ms, bl.max_ms, pl.min_ms, pl.median_ms, pl.mean_ms, pl.max_ms};
-    COMM_TRY(comm_allreduce_double_max(comm, tm, 8));
+    double tm[9] = {bl.min_ms, bl.median_ms, bl.mean_ms, bl.max_ms, pl.min_ms, pl.median_ms, pl.mean_ms, pl.max_ms,
+                    calib_max_local};
+    COMM_TRY(comm_allreduce_double_max(comm, tm, 9));
+
+    if (cfg.calibrate) {
+        // Gather every rank's diffs on rank 0 in rank order (main.cu:279-308).
+        std::vector<double> all = calib_diffs_local;
+        if (world_rank == 0) {
+            for (int r = 1; r < world_size; ++r) {
+                long long n = 0;
+                COMM_TRY(comm_recv_host(comm, &n, sizeof(n), r));
+                std::vector<double> part((size_t)n);
+                COMM_TRY(comm_recv_host(comm, part.data(), sizeof(double) * (size_t)n, r));
+                all.insert(all.end(), part.begin(), part.end());
+            }
+            std::ofstream ofs(cfg.calib_diffs_path);
+            if (ofs.is_open()) {
+                ofs << "abs_diff\n";
+                ofs << std::scientific << std::setprecision(8);
+                for (double d : all) ofs << d << "\n";
+                std::cout << "Calibration diffs written : " << cfg.calib_diffs_path << "  (" << all.size()
+                          << " samples)\n";
+            }
+        } else {
+            long long n = (long long)calib_diffs_local.size();
+            COMM_TRY(comm_send_host(comm, &n, sizeof(n), 0));
+            COMM_TRY(comm_send_host(comm, calib_diffs_local.data(), sizeof(double) * (size_t)n, 0));
+        }
+    }
 
     if (world_rank == 0) {
         abft_metrics m{};
@@ -375,7 +437,7 @@ int main(int argc, char** argv) {
         copy_cstr(m.inject, sizeof(m.inject), cfg.inject);
         copy_cstr(m.swifi_zone, sizeof(m.swifi_zone), cfg.swifi_zone);
         m.baseline_only = cfg.baseline_only;
-        m.calibrate = 0;
+        m.calibrate = cfg.calibrate ? 1 : 0;
         m.M = cfg.M; m.K = cfg.K; m.N = cfg.N;
         m.Pr = cfg.Pr; m.Pc = cfg.Pc;
         m.frags_per_rank = F;
@@ -386,6 +448,11 @@ int main(int argc, char** argv) {
         m.protected_ = abft_timing{tm[4], tm[5], tm[6], tm[7], pl.n_samples};
         for (int i = 0; i < 4; ++i) m.cm[i] = agg[i];
         m.n_restored = agg[4];
+        if (cfg.calibrate) {
+            m.calib_max_diff = tm[8];
+            m.calib_safety_factor = cfg.calibration_safety_factor;
+            m.calib_suggested_tau = tm[8] * cfg.calibration_safety_factor;
+        }
         ABFT_TRY(abft_metrics_finalize(&m));
         std::vector<char> buf(8192);
         abft_metrics_report(&m, buf.data(), buf.size());

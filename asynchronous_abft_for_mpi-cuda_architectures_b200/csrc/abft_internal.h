@@ -34,6 +34,11 @@ struct InjectLog {
     float before, after;
 };
 
+// Injection of one iteration, read on the device in graph mode (frag -1: none).
+struct InjectPlan {
+    int frag, row, col, bit;
+};
+
 struct PendingFix {
     int it, f, er, ec, injected, off;
     double rowdiff;
@@ -73,6 +78,7 @@ struct WsDev {
     DecisionLog* dlog; // [max_iters][F]
     InjectLog* ilog;   // [max_iters]
     PendingFix* pend;  // [max_iters * F]
+    InjectPlan* plan;  // [max_iters]
 };
 
 }  // namespace abft
@@ -97,17 +103,20 @@ int cuda_fail(cudaError_t e, const char* what);
 
 struct WsLayout {
     size_t colSumA, expRow, rowSumB, expCol, rec, ctr, vacc_s, vacc_t, vacc_m, vact, vd, vw, vcnt, lact, ld, lw, lcnt, dlog, ilog,
-        pend, total;
+        pend, plan, total;
 };
 WsLayout ws_layout(int M_b, int N_b, int K, int F, int nfmax, int max_iters);
 
 // Kernel launchers (enqueue only). Return ABFT_OK or a negative status.
 int launch_encode(abft_ws* ws, const float* dA, int64_t lda, const float* dB, int64_t ldb, cudaStream_t st,
                   int* launches);
+// plan_it >= 0 selects graph mode: the injection of iteration plan_it is read
+// from ws->d.plan on the device (verify applies it, log_inj logs it).
 int launch_verify(abft_ws* ws, const float* dC, int64_t ldc, int f, double tau, int injected, int it,
-                  cudaStream_t st);
+                  cudaStream_t st, int plan_it = -1, float add_delta = 0.f, int log_inj = 0,
+                  double* calib_out = nullptr);
 int launch_localize(abft_ws* ws, float* dC, int64_t ldc, int f, double tau, int injected, const float* dG,
-                    int64_t ldg, int it, int correct_mode, cudaStream_t st);
+                    int64_t ldg, int it, int correct_mode, cudaStream_t st, int plan_it = -1);
 int launch_drain(abft_ws* ws, float* dC0, float* dC1, int64_t ldc, const float* dG, int64_t ldg, int repeats,
                  cudaStream_t st);
 int launch_inject(float* dC, int64_t ldc, int row, int col, int mode, float delta, int bit, InjectLog* log,

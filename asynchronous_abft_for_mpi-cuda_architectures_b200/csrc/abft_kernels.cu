@@ -77,14 +77,15 @@ __device__ __forceinline__ void acc1(float x, double& s, float& t, uint32_t& m) 
 
 // Sequential double sum x[0] + x[stride] + ... (n terms) in ascending order,
 // starting from 0.0: the reference's per-thread loop. Warp-cooperative: lanes
-// prefetch 32 terms, every lane runs the same chain.
+// prefetch 32 terms (through L2: the verify kernel may have written one of
+// them in graph mode), every lane runs the same chain.
 __device__ double exact_chain(const float* __restrict__ x, long long stride, int n) {
     const int lane = threadIdx.x & 31;
     double s = 0.0;
-    float v = (lane < n) ? x[(long long)lane * stride] : 0.f;
+    float v = (lane < n) ? __ldcg(x + (long long)lane * stride) : 0.f;
     for (int i0 = 0; i0 < n; i0 += 32) {
         const int nx = i0 + 32 + lane;
-        const float vn = (nx < n) ? x[(long long)nx * stride] : 0.f;
+        const float vn = (nx < n) ? __ldcg(x + (long long)nx * stride) : 0.f;
         if (n - i0 >= 32) {
 #pragma unroll
             for (int r = 0; r < 32; ++r) s = __dadd_rn(s, (double)__shfl_sync(kFull, v, r));
@@ -238,7 +239,9 @@ __device__ int final_select(int n, double tau, const double* __restrict__ expv, 
 template <bool VEC>
 __global__ void __launch_bounds__(kThreads, 4)
     k_verify(const float* __restrict__ C, long long ldc, int M, int N, int rows_per, int total_ctas, int dw_in_smem,
-             const double* __restrict__ expv, double tau, int injected, int f, int F, int it, WsDev w) {
+             const double* __restrict__ expv, double tau, int injected, int f, int F, int it, WsDev w,
+             float* Cw, const InjectPlan* __restrict__ plan, int plan_it, float add_delta, int log_inj,
+             double* calib_out) {
     extern __shared__ __align__(16) unsigned char dsm[];
     __shared__ SelectSmem sel;
     double(*s_s)[kGroupCols] = reinterpret_cast<double(*)[kGroupCols]>(dsm);
@@ -254,6 +257,21 @@ __global__ void __launch_bounds__(kThreads, 4)
     double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
     float t0 = 0.f, t1 = 0.f, t2 = 0.f, t3 = 0.f;
     uint32_t m0 = kFull, m1 = kFull, m2 = kFull, m3 = kFull;
+
+    // Graph mode: this iteration's planned fault is applied here, by the one
+    // thread whose loads cover the element (nothing reads C between the SGEMM
+    // and this kernel, so the result equals injecting on the compute stream).
+    int inj_row = -1, inj_k = 0, inj_bit = -1;
+    if (plan != nullptr) {
+        const InjectPlan p = plan[plan_it];
+        injected = (p.frag == f) ? 1 : 0;
+        if (injected && p.row >= r0 && p.row < r1 && ((p.row - r0) % kWarps) == warp && p.col >= c0 &&
+            p.col < c0 + 4 && p.col < N) {
+            inj_row = p.row;
+            inj_k = p.col - c0;
+            inj_bit = p.bit;
+        }
+    }
 
     auto load = [&](int r) -> float4 {
         const float* p = C + (long long)r * ldc + c0;
@@ -284,6 +302,30 @@ __global__ void __launch_bounds__(kThreads, 4)
         for (int u = 0; u < kBatch; ++u) {
             const int rr = r + u * kWarps;
             v[u] = (rr < r1) ? load(rr) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        if (inj_row >= 0) {
+#pragma unroll
+            for (int u = 0; u < kBatch; ++u) {
+                if (r + u * kWarps == inj_row) {
+                    const float before = inj_k == 0 ? v[u].x : inj_k == 1 ? v[u].y : inj_k == 2 ? v[u].z : v[u].w;
+                    const float after = (inj_bit < 0) ? __fadd_rn(before, add_delta)
+                                                      : __uint_as_float(__float_as_uint(before) ^ (1u << inj_bit));
+                    if (inj_k == 0) v[u].x = after;
+                    else if (inj_k == 1) v[u].y = after;
+                    else if (inj_k == 2) v[u].z = after;
+                    else v[u].w = after;
+                    Cw[(long long)inj_row * ldc + c0 + inj_k] = after;
+                    if (log_inj) {
+                        InjectLog& L = w.ilog[plan_it];
+                        L.frag = f;
+                        L.row = inj_row;
+                        L.col = c0 + inj_k;
+                        L.bit = inj_bit;
+                        L.before = before;
+                        L.after = after;
+                    }
+                }
+            }
         }
 #pragma unroll
         for (int u = 0; u < kBatch; ++u) acc(v[u]);
@@ -352,6 +394,22 @@ __global__ void __launch_bounds__(kThreads, 4)
     }
     __syncthreads();
 
+    if (calib_out != nullptr) {
+        // Calibration (pass_calibrate, pipeline/passes.cuh:66-84): every
+        // |actualRow - expectedRow| exactly, uncertified columns re-summed in
+        // the reference's order; no detection, no counters.
+        for (int j = warp; j < N; j += kWarps) {
+            if (ww[j] != 0.0) {
+                const double S = exact_chain(C + j, ldc, M);
+                if (lane == 0) dd[j] = fabs(S - expv[j]);
+            }
+        }
+        __syncthreads();
+        for (int j = tid; j < N; j += kThreads) calib_out[j] = dd[j];
+        if (tid == 0) *w.vcnt = 0;
+        return;
+    }
+
     // The reference's detection (k_detect_row) on exact values.
     const int ec = final_select<false>(
         N, tau, expv, w.vact, dd, ww, [&](int j) { return exact_chain(C + j, ldc, M); }, sel);
@@ -382,10 +440,11 @@ template <bool VEC>
 __global__ void __launch_bounds__(kThreads)
     k_localize(float* C, long long ldc, int M, int N, int rows_per, int nblocks, const double* __restrict__ expc,
                double tau, int injected, const float* __restrict__ G, long long ldg, int frag_off, int f, int F,
-               int it, int drain, int pend_cap, WsDev w) {
+               int it, int drain, int pend_cap, WsDev w, const InjectPlan* __restrict__ plan, int plan_it) {
     __shared__ SelectSmem sel;
     const int ec = __ldcg(&w.rec[f].errcol);
     if (ec < 0) return;
+    if (plan != nullptr) injected = (plan[plan_it].frag == f) ? 1 : 0;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int r0 = blockIdx.x * rows_per;
     const int r1 = min(M, r0 + rows_per);
@@ -679,6 +738,8 @@ void verify_geometry(int sms, int M, int N, int& groups, int& chunks, int& rows_
     if (chunks > kMaxChunks) chunks = kMaxChunks;
     rows_per = (M + chunks - 1) / chunks;
     rows_per = ((rows_per + kWarps - 1) / kWarps) * kWarps;
+    // at least one full batch per warp: bounds the atomics per accumulator to M / 64
+    rows_per = std::max(rows_per, kBatch * kWarps);
     chunks = (M + rows_per - 1) / rows_per;
 }
 
@@ -750,7 +811,7 @@ int launch_encode(abft_ws* ws, const float* dA, int64_t lda, const float* dB, in
 }
 
 int launch_verify(abft_ws* ws, const float* dC, int64_t ldc, int f, double tau, int injected, int it,
-                  cudaStream_t st) {
+                  cudaStream_t st, int plan_it, float add_delta, int log_inj, double* calib_out) {
     const int M = ws->M_b, N = ws->counts[f];
     const float* Cf = dC + ws->offsets[f];
     if (int rc = ensure_kernel_attrs(ws->device)) return rc;
@@ -764,17 +825,21 @@ int launch_verify(abft_ws* ws, const float* dC, int64_t ldc, int f, double tau, 
     const int dw_in_smem = (16LL * N <= kVerifySmemMax) ? 1 : 0;
     const int smem = dw_in_smem ? std::max(reduce_bytes, 16 * N) : reduce_bytes;
     const int total = groups * chunks;
+    const InjectPlan* plan = (plan_it >= 0) ? ws->d.plan : nullptr;
+    float* Cw = const_cast<float*>(Cf);
     if (vec)
         k_verify<true><<<grid, kThreads, smem, st>>>(Cf, ldc, M, N, rows_per, total, dw_in_smem, expv, tau,
-                                                     injected, f, ws->F, it, ws->d);
+                                                     injected, f, ws->F, it, ws->d, Cw, plan, plan_it, add_delta,
+                                                     log_inj, calib_out);
     else
         k_verify<false><<<grid, kThreads, smem, st>>>(Cf, ldc, M, N, rows_per, total, dw_in_smem, expv, tau,
-                                                      injected, f, ws->F, it, ws->d);
+                                                      injected, f, ws->F, it, ws->d, Cw, plan, plan_it, add_delta,
+                                                      log_inj, calib_out);
     return check_launch("verify");
 }
 
 int launch_localize(abft_ws* ws, float* dC, int64_t ldc, int f, double tau, int injected, const float* dG,
-                    int64_t ldg, int it, int correct_mode, cudaStream_t st) {
+                    int64_t ldg, int it, int correct_mode, cudaStream_t st, int plan_it) {
     const int M = ws->M_b, N = ws->counts[f];
     float* Cf = dC + ws->offsets[f];
     // about 64 KB of C per CTA, whole warps of rows
@@ -794,10 +859,12 @@ int launch_localize(abft_ws* ws, float* dC, int64_t ldc, int f, double tau, int 
     }
     if (vec)
         k_localize<true><<<nblocks, kThreads, 0, st>>>(Cf, ldc, M, N, rows_per, nblocks, expc, tau, injected, dG,
-                                                       ldg, ws->offsets[f], f, ws->F, it, drain, cap, ws->d);
+                                                       ldg, ws->offsets[f], f, ws->F, it, drain, cap, ws->d,
+                                                       plan_it >= 0 ? ws->d.plan : nullptr, plan_it);
     else
         k_localize<false><<<nblocks, kThreads, 0, st>>>(Cf, ldc, M, N, rows_per, nblocks, expc, tau, injected, dG,
-                                                        ldg, ws->offsets[f], f, ws->F, it, drain, cap, ws->d);
+                                                        ldg, ws->offsets[f], f, ws->F, it, drain, cap, ws->d,
+                                                        plan_it >= 0 ? ws->d.plan : nullptr, plan_it);
     return check_launch("localize");
 }
 
@@ -918,10 +985,10 @@ int launch_verify_static(const float* Cf, int64_t ldc, int M, int N, const doubl
     const int total = groups * chunks;
     if (vec)
         k_verify<true><<<grid, kThreads, smem, st>>>(Cf, ldc, M, N, rows_per, total, 1, expv, tau, injected, 0, 1,
-                                                     -1, w);
+                                                     -1, w, nullptr, nullptr, 0, 0.f, 0, nullptr);
     else
         k_verify<false><<<grid, kThreads, smem, st>>>(Cf, ldc, M, N, rows_per, total, 1, expv, tau, injected, 0, 1,
-                                                      -1, w);
+                                                      -1, w, nullptr, nullptr, 0, 0.f, 0, nullptr);
     if (int rc = check_launch("verify (static scratch)")) return rc;
     k_static_copyout<<<1, 32, 0, st>>>(w.rec, w.ctr, errcol, rowdiff, cm);
     return check_launch("verify copy-out");

@@ -17,6 +17,7 @@
 #include <cublas_v2.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <chrono>
 #include <new>
 #include <string>
@@ -51,6 +52,13 @@ struct abft_session {
     int profile = 0;
     int max_iters = 0;
     int last_launches = 0;
+    // graph mode: one captured loop, replayed while its shape stays the same
+    cudaGraphExec_t gexec = nullptr;
+    int g_repeats = -1, g_mode = -1, g_correct = -1, g_log = -1, g_launches = 0, g_vlaunches = 0;
+    float g_delta = 0.f;
+    InjectPlan* plan_host = nullptr;  // pinned, max_iters entries
+    cudaGraphExec_t bexec = nullptr;  // graph of the baseline pass
+    int b_repeats = -1;
 };
 
 namespace {
@@ -97,8 +105,10 @@ struct Plan {
 };
 
 // Enqueue `repeats` protected iterations on the two streams (no host sync).
+// graph = true: the injection is read from the device plan table by the verify
+// kernel (capturable, the same graph serves every trial).
 int enqueue_loop(abft_session* s, const abft_online_args* a, const std::vector<Plan>& plan, int* launches,
-                 int* vlaunches) {
+                 int* vlaunches, bool graph = false) {
     const bool inject_on = (a->mode == ABFT_INJECT_ADD || a->mode == ABFT_INJECT_SWIFI);
     const bool do_localize = inject_on;
     bool used[2] = {false, false};
@@ -110,7 +120,7 @@ int enqueue_loop(abft_session* s, const abft_online_args* a, const std::vector<P
         const int log_it = (a->log && it < s->max_iters) ? it : -1;
         for (int f = 0; f < s->F; ++f) {
             RC(sgemm_frag(s, dC, f));
-            if (f == plan[it].frag) {
+            if (!graph && f == plan[it].frag) {
                 InjectLog* lg = (log_it >= 0) ? s->ws->d.ilog + log_it : nullptr;
                 const int mode = (a->mode == ABFT_INJECT_ADD) ? ABFT_INJECT_ADD : ABFT_INJECT_SWIFI;
                 RC(launch_inject(dC + s->offsets[f], s->ldc, plan[it].row, plan[it].col, mode, a->add_delta,
@@ -122,15 +132,19 @@ int enqueue_loop(abft_session* s, const abft_online_args* a, const std::vector<P
         for (int f = 0; f < s->F; ++f) {
             const int injected = (f == plan[it].frag) ? 1 : 0;
             CK(cudaStreamWaitEvent(s->verify, s->compute_done[f], 0));
-            const bool prof = s->profile && (size_t)(2 * nv + 1) < s->vprof.size();
+            const bool prof = !graph && s->profile && (size_t)(2 * nv + 1) < s->vprof.size();
             if (prof) CK(cudaEventRecord(s->vprof[2 * nv], s->verify));
-            RC(launch_verify(s->ws, dC, s->ldc, f, s->tau[f], injected, log_it, s->verify));
+            if (graph)
+                RC(launch_verify(s->ws, dC, s->ldc, f, s->tau[f], 0, log_it, s->verify, it, a->add_delta,
+                                 (a->log && inject_on) ? 1 : 0));
+            else
+                RC(launch_verify(s->ws, dC, s->ldc, f, s->tau[f], injected, log_it, s->verify));
             if (prof) CK(cudaEventRecord(s->vprof[2 * nv + 1], s->verify));
             ++nl;
             ++nv;
             if (do_localize) {
                 RC(launch_localize(s->ws, dC, s->ldc, f, s->tau[f], injected, s->dG, s->ldg, it, a->correct_mode,
-                                   s->verify));
+                                   s->verify, graph ? it : -1));
                 ++nl;
             }
         }
@@ -155,6 +169,55 @@ int make_plan(abft_session* s, const abft_online_args* a, std::vector<Plan>& pla
     return ABFT_OK;
 }
 
+void drop_graph(abft_session* s) {
+    if (s->gexec) cudaGraphExecDestroy(s->gexec);
+    s->gexec = nullptr;
+    s->g_repeats = -1;
+}
+
+// Capture the loop once for this shape (repeats, mode, correction, logging,
+// fault size); thresholds and the golden pointer are baked in, so setting
+// them drops the graph.
+int build_graph(abft_session* s, const abft_online_args* a, const std::vector<Plan>& plan) {
+    if (s->gexec && s->g_repeats == a->repeats && s->g_mode == a->mode && s->g_correct == a->correct_mode &&
+        s->g_log == a->log && s->g_delta == a->add_delta)
+        return ABFT_OK;
+    drop_graph(s);
+    CK(cudaStreamBeginCapture(s->compute, cudaStreamCaptureModeThreadLocal));
+    int nl = 0, nv = 0;
+    int rc = ABFT_OK;
+    cudaError_t e = cudaEventRecord(s->cjoin, s->compute);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(s->verify, s->cjoin, 0);
+    if (e != cudaSuccess) rc = cuda_fail(e, "graph fork");
+    if (rc == ABFT_OK) rc = enqueue_loop(s, a, plan, &nl, &nv, true);
+    if (rc == ABFT_OK) {
+        e = cudaEventRecord(s->vjoin, s->verify);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(s->compute, s->vjoin, 0);
+        if (e != cudaSuccess) rc = cuda_fail(e, "graph join");
+    }
+    cudaGraph_t g = nullptr;
+    e = cudaStreamEndCapture(s->compute, &g);
+    if (rc == ABFT_OK && e != cudaSuccess) rc = cuda_fail(e, "cudaStreamEndCapture");
+    if (rc == ABFT_OK) {
+        e = cudaGraphInstantiate(&s->gexec, g, 0);
+        if (e != cudaSuccess) {
+            s->gexec = nullptr;
+            rc = cuda_fail(e, "cudaGraphInstantiate");
+        }
+    }
+    if (g) cudaGraphDestroy(g);
+    (void)cudaGetLastError();
+    if (rc != ABFT_OK) return rc;
+    s->g_repeats = a->repeats;
+    s->g_mode = a->mode;
+    s->g_correct = a->correct_mode;
+    s->g_log = a->log;
+    s->g_delta = a->add_delta;
+    s->g_launches = nl;
+    s->g_vlaunches = nv;
+    return ABFT_OK;
+}
+
 int check_args(abft_session* s, const abft_online_args* a) {
     if (!a || a->repeats < 0 || (a->mode < ABFT_INJECT_NONE || a->mode > ABFT_INJECT_SWIFI) ||
         (a->correct_mode != ABFT_CORRECT_INLOOP && a->correct_mode != ABFT_CORRECT_DRAIN)) {
@@ -167,6 +230,10 @@ int check_args(abft_session* s, const abft_online_args* a) {
     }
     if (a->correct_mode == ABFT_CORRECT_DRAIN && a->mode != ABFT_INJECT_NONE && a->repeats > s->max_iters) {
         set_error("online: drain correction needs repeats <= max_iters");
+        return ABFT_ERR_ARG;
+    }
+    if (a->graph && a->repeats > s->max_iters) {
+        set_error("online: graph mode needs repeats <= max_iters (the device injection plan table)");
         return ABFT_ERR_ARG;
     }
     return ABFT_OK;
@@ -259,6 +326,8 @@ int abft_session_create(const abft_session_cfg* c, abft_session** out) {
     if (e != cudaSuccess) return fail(cuda_fail(e, "event create"));
     int rc = abft_ws_create(s->M_b, s->N_b, s->K, s->F, c->counts, c->offsets, c->max_iters, nullptr, 0, &s->ws);
     if (rc != ABFT_OK) return fail(rc);
+    e = cudaMallocHost(&s->plan_host, sizeof(InjectPlan) * (size_t)std::max(c->max_iters, 1));
+    if (e != cudaSuccess) return fail(cuda_fail(e, "pinned plan buffer"));
     rc = gemm_warmup(s);
     if (rc != ABFT_OK) return fail(rc);
     *out = s;
@@ -269,6 +338,9 @@ int abft_session_destroy(abft_session* s) {
     if (!s) return ABFT_OK;
     if (s->compute) cudaStreamSynchronize(s->compute);
     if (s->verify) cudaStreamSynchronize(s->verify);
+    drop_graph(s);
+    if (s->bexec) cudaGraphExecDestroy(s->bexec);
+    if (s->plan_host) cudaFreeHost(s->plan_host);
     for (auto e : s->compute_done)
         if (e) cudaEventDestroy(e);
     for (auto e : s->vprof)
@@ -291,6 +363,7 @@ int abft_session_set_tau(abft_session* s, const double* tau) {
         return ABFT_ERR_ARG;
     }
     s->tau.assign(tau, tau + s->F);
+    drop_graph(s);
     return ABFT_OK;
 }
 
@@ -301,6 +374,7 @@ int abft_session_set_golden(abft_session* s, const float* dG, int64_t ldg) {
     }
     s->dG = dG;
     s->ldg = dG ? ldg : 0;
+    drop_graph(s);
     return ABFT_OK;
 }
 
@@ -320,16 +394,42 @@ int abft_session_encode(abft_session* s, double* encode_ms) {
     return ABFT_OK;
 }
 
-int abft_session_baseline(abft_session* s, int repeats, double* device_ms, double* host_ms) {
+int abft_session_baseline(abft_session* s, int repeats, int graph, double* device_ms, double* host_ms) {
     if (!s || repeats < 0) {
         set_error("abft_session_baseline: bad argument");
         return ABFT_ERR_ARG;
     }
     CK(cudaStreamSynchronize(s->compute));
+    if (graph && (!s->bexec || s->b_repeats != repeats)) {
+        if (s->bexec) cudaGraphExecDestroy(s->bexec);
+        s->bexec = nullptr;
+        CK(cudaStreamBeginCapture(s->compute, cudaStreamCaptureModeThreadLocal));
+        int rc = ABFT_OK;
+        for (int it = 0; it < repeats && rc == ABFT_OK; ++it)
+            for (int f = 0; f < s->F && rc == ABFT_OK; ++f) rc = sgemm_frag(s, s->dC[0], f);
+        cudaGraph_t g = nullptr;
+        cudaError_t e = cudaStreamEndCapture(s->compute, &g);
+        if (rc == ABFT_OK && e != cudaSuccess) rc = cuda_fail(e, "cudaStreamEndCapture (baseline)");
+        if (rc == ABFT_OK) {
+            e = cudaGraphInstantiate(&s->bexec, g, 0);
+            if (e != cudaSuccess) {
+                s->bexec = nullptr;
+                rc = cuda_fail(e, "cudaGraphInstantiate (baseline)");
+            }
+        }
+        if (g) cudaGraphDestroy(g);
+        (void)cudaGetLastError();
+        if (rc != ABFT_OK) return rc;
+        s->b_repeats = repeats;
+    }
     const auto h0 = std::chrono::high_resolution_clock::now();
     CK(cudaEventRecord(s->t0, s->compute));
-    for (int it = 0; it < repeats; ++it)
-        for (int f = 0; f < s->F; ++f) RC(sgemm_frag(s, s->dC[0], f));
+    if (graph) {
+        CK(cudaGraphLaunch(s->bexec, s->compute));
+    } else {
+        for (int it = 0; it < repeats; ++it)
+            for (int f = 0; f < s->F; ++f) RC(sgemm_frag(s, s->dC[0], f));
+    }
     CK(cudaEventRecord(s->t1, s->compute));
     CK(cudaEventSynchronize(s->t1));
     const auto h1 = std::chrono::high_resolution_clock::now();
@@ -358,13 +458,27 @@ int abft_session_online(abft_session* s, const abft_online_args* a, abft_online_
     CK(cudaStreamSynchronize(s->verify));
     CK(cudaStreamSynchronize(s->compute));
 
+    int nl = 0, nv = 0;
+    if (a->graph) {
+        RC(build_graph(s, a, plan));
+        for (int it = 0; it < a->repeats; ++it)
+            s->plan_host[it] = InjectPlan{plan[it].frag, plan[it].row, plan[it].col, plan[it].bit};
+        CK(cudaMemcpyAsync(s->ws->d.plan, s->plan_host, sizeof(InjectPlan) * a->repeats, cudaMemcpyHostToDevice,
+                           s->compute));
+        RC(abft_ws_reset_counters(s->ws, s->compute));
+        nl = s->g_launches;
+        nv = s->g_vlaunches;
+    }
     const auto h0 = std::chrono::high_resolution_clock::now();
     CK(cudaEventRecord(s->t0, s->compute));
-    CK(cudaStreamWaitEvent(s->verify, s->t0, 0));
-    int nl = 0, nv = 0;
-    RC(enqueue_loop(s, a, plan, &nl, &nv));
-    CK(cudaEventRecord(s->vjoin, s->verify));
-    CK(cudaStreamWaitEvent(s->compute, s->vjoin, 0));
+    if (a->graph) {
+        CK(cudaGraphLaunch(s->gexec, s->compute));
+    } else {
+        CK(cudaStreamWaitEvent(s->verify, s->t0, 0));
+        RC(enqueue_loop(s, a, plan, &nl, &nv));
+        CK(cudaEventRecord(s->vjoin, s->verify));
+        CK(cudaStreamWaitEvent(s->compute, s->vjoin, 0));
+    }
     CK(cudaEventRecord(s->t1, s->compute));
     CK(cudaEventSynchronize(s->t1));
     const auto h1 = std::chrono::high_resolution_clock::now();

@@ -105,6 +105,15 @@ def verify(ws, C, f, tau, injected=False, it=-1, stream=None):
          _stream(stream))
 
 
+def calibrate(ws, C, f, out=None, stream=None):
+    """|actualRow - expectedRow| of every column of fragment f (float64 CUDA tensor)."""
+    _check_tile(C, ws.M_b, ws.N_b, "C")
+    if out is None:
+        out = torch.empty(int(ws.counts[f]), dtype=torch.float64, device=C.device)
+    call("abft_calibrate", ws.handle, C.data_ptr(), C.stride(0), int(f), out.data_ptr(), _stream(stream))
+    return out
+
+
 def localize_correct(ws, C, f, tau, injected=False, golden=None, it=-1, correct_mode=CORRECT_INLOOP, stream=None):
     """Gated localisation and correction of fragment f."""
     _check_tile(C, ws.M_b, ws.N_b, "C")

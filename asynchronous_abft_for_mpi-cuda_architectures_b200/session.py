@@ -87,13 +87,15 @@ class OnlineSession:
             call("abft_session_encode", self.handle, ctypes.byref(ms))
         return ms.value
 
-    def baseline(self, repeats):
+    def baseline(self, repeats, graph=False):
+        """repeats x F unprotected SGEMMs (the reference's pass_baseline); (device_ms, host_ms)."""
         dms, hms = ctypes.c_double(), ctypes.c_double()
         with torch.cuda.device(self.device):
-            call("abft_session_baseline", self.handle, int(repeats), ctypes.byref(dms), ctypes.byref(hms))
+            call("abft_session_baseline", self.handle, int(repeats), int(bool(graph)), ctypes.byref(dms),
+                 ctypes.byref(hms))
         return dms.value, hms.value
 
-    def _args(self, mode, zone, add_delta, base_seed, rank, repeats, correct, log, profile=False):
+    def _args(self, mode, zone, add_delta, base_seed, rank, repeats, correct, log, profile=False, graph=False):
         lo, hi = host.swifi_zone_range(zone)
         a = OnlineArgs()
         a.mode = host.MODES[mode] if isinstance(mode, str) else int(mode)
@@ -105,6 +107,7 @@ class OnlineSession:
         a.correct_mode = CORRECT_DRAIN if correct == "drain" else CORRECT_INLOOP
         a.log = int(bool(log))
         a.profile = int(bool(profile))
+        a.graph = int(bool(graph))
         return a
 
     @staticmethod
@@ -114,15 +117,16 @@ class OnlineSession:
                     verify_ms_sum=r.verify_ms_sum, verify_ms_max=r.verify_ms_max)
 
     def online(self, mode="none", zone="any", add_delta=ADD_FAULT_DELTA, base_seed=0, rank=0, repeats=1,
-               correct="inloop", log=False, profile=False):
+               correct="inloop", log=False, profile=False, graph=False):
         """repeats protected iterations; returns timings, confusion matrix and restore count.
 
         profile=True brackets every verify launch with CUDA events on the verify
-        stream (verify_ms_sum / verify_ms_max in the result).
+        stream (verify_ms_sum / verify_ms_max in the result). graph=True replays
+        the loop as a CUDA graph (captured on first use for this shape).
         """
         if self.tau is None:
             raise RuntimeError("set_tau() first")
-        a = self._args(mode, zone, add_delta, base_seed, rank, repeats, correct, log, profile)
+        a = self._args(mode, zone, add_delta, base_seed, rank, repeats, correct, log, profile, graph)
         r = OnlineResult()
         with torch.cuda.device(self.device):
             call("abft_session_online", self.handle, ctypes.byref(a), ctypes.byref(r))

@@ -47,6 +47,7 @@ def parse():
     p.add_argument("--seed-b", type=int, default=987654)
     p.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU-baseline work")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-graph", action="store_true", help="enqueue the loop from the host every trial")
     p.add_argument("--no-cpu", action="store_true")
     return p.parse_args()
 
@@ -61,6 +62,7 @@ def workload(args, Pr, Pc):
         "inject": args.mode, "swifi_zone": args.zone,
         "l2": "inputs larger than L2 (A, B, 2 x C per rank = 256 MiB > 126 MB)",
         "parallelism": f"{Pr}x{Pc} output-tile grid, one rank per GPU",
+        "loop": "host-enqueued" if args.no_graph else "CUDA graph per trial",
     }
 
 
@@ -257,8 +259,9 @@ def run_ours(args):
     base = args.seed_a + args.seed_b
 
     for w in range(args.warmup):
-        s.baseline(args.iters)
-        s.online(args.mode, args.zone, base_seed=base + w * 31337, rank=rank, repeats=args.iters)
+        s.baseline(args.iters, graph=not args.no_graph)
+        s.online(args.mode, args.zone, base_seed=base + w * 31337, rank=rank, repeats=args.iters,
+                 graph=not args.no_graph)
 
     def region(fn):
         dist_mod.barrier(dev)
@@ -268,11 +271,11 @@ def run_ours(args):
         dist_mod.barrier(dev)
         return out
 
-    b_ms = region(lambda i: s.baseline(args.iters)[0])
+    b_ms = region(lambda i: s.baseline(args.iters, graph=not args.no_graph)[0])
     sampler = ClockSampler(torch, dev)
     sampler.start()
     p_res = region(lambda i: s.online(args.mode, args.zone, base_seed=base + (args.warmup + i) * 31337, rank=rank,
-                                      repeats=args.iters))
+                                      repeats=args.iters, graph=not args.no_graph))
     clocks = sampler.stop()
     p_ms = [r["device_ms"] for r in p_res]
     cm = np.sum([r["cm"] for r in p_res], axis=0).tolist()
@@ -333,7 +336,8 @@ def run_ours(args):
             "overhead_pct": (med_p / med_b - 1.0) * 100.0,
             "overhead_pct_total": (total_p / sum(b_max) - 1.0) * 100.0,
             "baseline_tflops": base_tf,
-            "baseline_kind": "unprotected cuBLAS SGEMM, same F fragments (pass_baseline)",
+            "baseline_kind": "unprotected cuBLAS SGEMM, same F fragments (pass_baseline)"
+                             + ("" if args.no_graph else ", CUDA graph per trial"),
             "encode_ms": encode_ms,
             "confusion_matrix": {"TP": int(cm_all[0]), "TN": int(cm_all[1]), "FP": int(cm_all[2]),
                                  "FN": int(cm_all[3]), "restored": int(cm_all[4])},

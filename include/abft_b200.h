@@ -128,6 +128,12 @@ int abft_encode(abft_ws* ws, const float* dA, int64_t lda, const float* dB, int6
  * rank tile's base pointer. `it` indexes the decision log (-1 = no log). */
 int abft_verify(abft_ws* ws, const float* dC, int64_t ldc, int f, double tau, int injected, int it, void* stream);
 
+/* Calibration of fragment f (pass_calibrate, pipeline/passes.cuh:66-84):
+ * writes |actualRow[j] - expectedRow[j]| for every column j of the fragment
+ * into the device array dDiff[counts[f]], bit-identical to the reference's
+ * host loop; no detection, no counter update. */
+int abft_calibrate(abft_ws* ws, const float* dC, int64_t ldc, int f, double* dDiff, void* stream);
+
 /* Verify one fragment without allocating anything. No counterpart in the
  * reference: it exists for callers that must not allocate device memory while
  * they run - a fault-tolerance hook called from inside another library's hot
@@ -209,6 +215,11 @@ typedef struct abft_online_args {
     int correct_mode; /* ABFT_CORRECT_INLOOP / ABFT_CORRECT_DRAIN           */
     int log;          /* 1: fill the decision + injection logs              */
     int profile;      /* 1: time every verify launch with CUDA events       */
+    int graph;        /* 1: run the loop as a CUDA graph captured once per
+                         (repeats, mode, correction, log, add_delta) and
+                         replayed; the injection plan goes to a device table
+                         and the verify kernel applies the fault. Needs
+                         repeats <= max_iters; ignores profile.            */
 } abft_online_args;
 
 typedef struct abft_online_result {
@@ -232,8 +243,10 @@ int abft_session_set_tau(abft_session* s, const double* tau);
 int abft_session_set_golden(abft_session* s, const float* dGolden, int64_t ldg);
 /* The untimed encode of pass_online_loop (pipeline/passes.cuh:118-128). */
 int abft_session_encode(abft_session* s, double* encode_ms);
-/* pass_baseline, pipeline/passes.cuh:14-35: repeats x F SGEMMs into dC0. */
-int abft_session_baseline(abft_session* s, int repeats, double* device_ms, double* host_ms);
+/* pass_baseline, pipeline/passes.cuh:14-35: repeats x F SGEMMs into dC0.
+ * graph = 1 replays them as a CUDA graph (captured once per repeats), the
+ * unprotected counterpart of abft_online_args.graph. */
+int abft_session_baseline(abft_session* s, int repeats, int graph, double* device_ms, double* host_ms);
 /* pass_online_loop, pipeline/passes.cuh:90-227 (timed part). */
 int abft_session_online(abft_session* s, const abft_online_args* args, abft_online_result* res);
 /* Injection log of the last online call: it_count x {frag, row, col, bit}

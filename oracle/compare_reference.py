@@ -54,8 +54,10 @@ def main():
             continue
         common = ["--repeats", "5", "--samples", "3", "--warmups", "1"] if big else \
             ["--repeats", "20", "--samples", "5", "--warmups", "2"]
-        for name, binary in (("reference (sm_100a build)", REF), ("this project", OURS)):
-            row, err = run(binary, args, common)
+        runs = [("reference (sm_100a build)", REF, []), ("this project", OURS, []),
+                ("this project, --graph", OURS, ["--graph"])]
+        for name, binary, extra in runs:
+            row, err = run(binary, args + extra, common)
             if row is None:
                 print(f"| {label} | {name} | failed: {err.strip()} | | | | |")
                 continue

@@ -31,6 +31,8 @@ CASES = [
     ["2048", "--inject", "swifi", "--swifi-zone", "sig_high", "--threshold", "0.02", "--frags-per-rank", "8"],
     ["1024", "--inject", "swifi", "--reseed-per-trial", "--threshold", "0.01024"],
     ["4096", "1024", "2048", "--inject", "add", "--threshold", "0.04", "--frag-cap", "1000000"],
+    ["1024", "--calibrate"],
+    ["1100", "300", "1030", "--calibrate", "--calibration-safety", "4", "--frags-per-rank", "3"],
 ]
 
 
@@ -39,7 +41,9 @@ def run(binary, args, csv_path, env_extra=None):
     env.update(env_extra or {})
     for k in ("RANK", "WORLD_SIZE", "LOCAL_RANK"):
         env.pop(k, None)
-    r = subprocess.run([binary] + args + ["--csv", csv_path], capture_output=True, text=True, timeout=600, env=env)
+    diffs = csv_path + ".diffs"
+    r = subprocess.run([binary] + args + ["--csv", csv_path, "--calib-diffs", diffs], capture_output=True, text=True,
+                       timeout=600, env=env)
     assert r.returncode == 0, (binary, r.stdout[-2000:], r.stderr[-2000:])
     with open(csv_path) as f:
         rows = list(csv.DictReader(f))
@@ -56,7 +60,14 @@ def test_driver_matches_reference_binary(case, tmp_path):
     for k in ref:
         if k not in TIMING_COLS:
             assert ours[k] == ref[k], (k, ours[k], ref[k])
-    assert "TP / TN / FP / FN" in out_ours
+    if "--calibrate" in case:
+        a = open(str(tmp_path / "ours.csv.diffs")).read()
+        b = open(str(tmp_path / "ref.csv.diffs")).read()
+        assert a.splitlines()[0] == "abs_diff" and len(a.splitlines()) > 1000
+        assert a == b  # every |actual - expected|, printed with 8 significant digits
+        assert "Suggested threshold" in out_ours
+    else:
+        assert "TP / TN / FP / FN" in out_ours
 
 
 def test_driver_rejects_bad_flags(tmp_path):

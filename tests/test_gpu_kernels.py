@@ -265,3 +265,30 @@ def test_bad_arguments_raise(abft, torch_cuda):
     with pytest.raises(abft.AbftError):
         abft.kernels.inject_bitflip(C, 0, 0, 32)
     ws.close()
+
+
+@pytest.mark.parametrize("shape", [(257, 129, 515, 4), (1024, 1024, 1024, 4), (4096, 8, 256, 1)])
+def test_calibrate_exact_diffs(shape, abft, orc, torch_cuda):
+    """|actualRow - expectedRow| of every column (pass_calibrate), bit-exact,
+    including columns whose parallel sum is not certified."""
+    torch = torch_cuda
+    M, K, N, F = shape
+    A, B = tiles(orc, M, K, N, 61, 62)
+    counts, offsets = orc.split_dim(N, F)
+    C = product_f64(A, B)
+    if M == 4096:  # force uncertified columns: one huge term followed by many tiny ones
+        C[0, 3] = 2.0 ** 30
+        C[1:, 3] = 2.0 ** -27
+        C[7, 100] = 1.0e30
+    ws = abft.kernels.Workspace(M, N, K, counts, offsets)
+    dA, dB, dC = to_dev(torch, A), to_dev(torch, B), to_dev(torch, C)
+    abft.kernels.encode(ws, dA, dB)
+    got = [abft.kernels.calibrate(ws, dC, f).cpu().numpy() for f in range(F)]
+    torch.cuda.synchronize()
+    _, expRow, _, _ = orc.encode(A, B, counts, offsets)
+    act = orc.actual_row(C)
+    want = np.abs(act - expRow)
+    for f in range(F):
+        w = want[offsets[f]:offsets[f] + counts[f]]
+        assert np.array_equal(got[f].view(np.uint64), w.view(np.uint64))
+    ws.close()

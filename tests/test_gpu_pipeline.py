@@ -131,3 +131,32 @@ def test_baseline_and_run_host(abft, orc):
     assert np.array_equal(hC.numpy().view(np.uint32), o["buf0"].view(np.uint32))
     assert res["e2e_ms"] > 0
     s.close()
+
+
+@pytest.mark.parametrize("mode,zone,correct", [("swifi", "any", "inloop"), ("add", "any", "inloop"),
+                                                ("none", "any", "inloop"), ("swifi", "exponent", "drain")])
+def test_graph_mode_matches_oracle(mode, zone, correct, abft, orc):
+    """The loop replayed as a CUDA graph (injection applied inside the verify
+    kernel from the device plan table) gives the same decisions, logs and
+    buffers, trial after trial with different seeds."""
+    s, A, B, counts, offsets, tau, C0 = make_session(abft, orc, 1024, 512, 1024, 4, 3, 4, max_iters=12)
+    golden = torch.from_numpy(C0).cuda() if mode == "swifi" else None
+    s.set_golden(golden)
+    for trial in range(3):
+        base = 777 + trial * 31337
+        res = s.online(mode, zone, base_seed=base, repeats=12, log=True, correct=correct, graph=True)
+        o = orc.online_loop(C0, A, B, counts, offsets, tau, mode, zone, 1.0e6, base, 0, 12,
+                            golden=C0 if mode == "swifi" else None)
+        compare(s, res, o, 12)
+    s.close()
+
+
+def test_graph_mode_uneven_and_small_fragments(abft, orc):
+    s, A, B, counts, offsets, tau, C0 = make_session(abft, orc, 1100, 300, 1030, 3, 5, 7, max_iters=9)
+    s.set_golden(torch.from_numpy(C0).cuda())
+    res = s.online("swifi", "any", base_seed=91, rank=3, repeats=9, log=True, graph=True)
+    o = orc.online_loop(C0, A, B, counts, offsets, tau, "swifi", "any", 1.0e6, 91, 3, 9, golden=C0)
+    compare(s, res, o, 9)
+    with pytest.raises(abft.AbftError):
+        s.online("add", repeats=10, graph=True)  # beyond the plan table
+    s.close()
