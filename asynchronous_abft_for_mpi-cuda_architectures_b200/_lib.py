@@ -49,7 +49,7 @@ class OnlineArgs(ctypes.Structure):
         ("mode", ctypes.c_int), ("zone_lo", ctypes.c_int), ("zone_hi", ctypes.c_int),
         ("add_delta", ctypes.c_float), ("base_seed", ctypes.c_uint64), ("rank", ctypes.c_int),
         ("repeats", ctypes.c_int), ("correct_mode", ctypes.c_int), ("log", ctypes.c_int),
-        ("profile", ctypes.c_int), ("graph", ctypes.c_int),
+        ("profile", ctypes.c_int), ("graph", ctypes.c_int), ("seed_scheme", ctypes.c_int),
     ]
 
 
@@ -107,6 +107,7 @@ SIGNATURES = {
     "abft_frag_thresholds": (_I, [_P, _I, _I, _I64, _P, _I64, _I, _IP, _IP, _D, _DP]),
     "abft_swifi_zone_range": (_I, [ctypes.c_char_p, _IP, _IP]),
     "abft_injection_plan": (_I, [_U64, _I, _I, _I, _I, _IP, _I, _I, _I, _IP, _IP, _IP, _IP]),
+    "abft_injection_plan_tile": (_I, [_U64, _I, _I, _IP, _IP, _I, _I, _I, _IP, _IP, _IP, _IP]),
     "abft_ws_bytes": (ctypes.c_size_t, [_I, _I, _I, _I, _IP, _I]),
     "abft_ws_create": (_I, [_I, _I, _I, _I, _IP, _IP, _I, _P, ctypes.c_size_t, ctypes.POINTER(_P)]),
     "abft_ws_destroy": (_I, [_P]),

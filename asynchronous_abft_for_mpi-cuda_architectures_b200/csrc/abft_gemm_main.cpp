@@ -50,6 +50,7 @@ struct Config {
     double relative_threshold = -1.0;  // tau = r * K * max|A| * max|B|
     bool csv_extra = false;
     bool graph = false;
+    int seed_scheme = ABFT_SEED_REFERENCE;
 };
 
 void print_help() {
@@ -83,6 +84,7 @@ void print_help() {
         "  --verify-priority {low|default|high}\n"
         "  --csv-extra                    append encode/verify columns to the CSV\n"
         "  --graph                        replay each trial's loop as a CUDA graph\n"
+        "  --inject-seed-mode {reference|json}  json: (i,j) uniform over the tile from seed 1 + iteration\n"
         "  --help                         this message\n";
 }
 
@@ -125,6 +127,12 @@ bool parse(int argc, char** argv, Config& c, std::string& err) {
             c.verify_priority = (m == "high") ? 1 : (m == "default" ? 0 : -1);
         } else if (a == "--csv-extra") c.csv_extra = true;
         else if (a == "--graph") c.graph = true;
+        else if (a == "--inject-seed-mode" && need(1)) {
+            std::string m = argv[++i];
+            if (m == "reference") c.seed_scheme = ABFT_SEED_REFERENCE;
+            else if (m == "json") c.seed_scheme = ABFT_SEED_TILE;
+            else { err = "--inject-seed-mode must be reference or json"; return false; }
+        }
         else if (a == "--help" || a == "-h") { print_help(); std::exit(0); }
         else if (!a.empty() && a[0] != '-') pos.push_back(std::atoi(argv[i]));
         else { err = "unknown or incomplete flag " + a; return false; }
@@ -377,7 +385,9 @@ int main(int argc, char** argv) {
         a.zone_lo = lo;
         a.zone_hi = hi;
         a.add_delta = cfg.add_delta;
-        a.base_seed = cfg.seed_a + cfg.seed_b + (unsigned long long)t * 31337ull;
+        a.base_seed = (cfg.seed_scheme == ABFT_SEED_TILE) ? 1ull
+                                                          : cfg.seed_a + cfg.seed_b + (unsigned long long)t * 31337ull;
+        a.seed_scheme = cfg.seed_scheme;
         a.rank = world_rank;
         a.repeats = cfg.repeats;
         a.correct_mode = cfg.correct_mode;

@@ -171,4 +171,32 @@ int abft_injection_plan(uint64_t base_seed, int rank, int it, int F, int M_b, co
     return ABFT_OK;
 }
 
+int abft_injection_plan_tile(uint64_t seed, int M_b, int F, const int* counts, const int* offsets, int mode,
+                             int zone_lo, int zone_hi, int* frag, int* row, int* col, int* bit) {
+    if (!frag || !row || !col || !bit || F < 1 || M_b < 1 || !counts || !offsets ||
+        (mode == ABFT_INJECT_SWIFI && (zone_lo < 0 || zone_hi > 31 || zone_lo > zone_hi))) {
+        set_error("abft_injection_plan_tile: bad argument");
+        return ABFT_ERR_ARG;
+    }
+    *frag = *row = *col = *bit = -1;
+    if (mode != ABFT_INJECT_ADD && mode != ABFT_INJECT_SWIFI) return ABFT_OK;
+    int N_b = 0;
+    for (int f = 0; f < F; ++f) N_b = std::max(N_b, offsets[f] + counts[f]);
+    std::mt19937_64 gen(seed);
+    std::uniform_int_distribution<int> rd(0, M_b - 1);
+    std::uniform_int_distribution<int> cd(0, N_b - 1);
+    *row = rd(gen);
+    const int j = cd(gen);
+    if (mode == ABFT_INJECT_SWIFI) {
+        std::uniform_int_distribution<int> bd(zone_lo, zone_hi);
+        *bit = bd(gen);
+    }
+    int fr = 0;
+    for (int f = 0; f < F; ++f)
+        if (j >= offsets[f] && j < offsets[f] + counts[f]) fr = f;
+    *frag = fr;
+    *col = j - offsets[fr];
+    return ABFT_OK;
+}
+
 }  // extern "C"

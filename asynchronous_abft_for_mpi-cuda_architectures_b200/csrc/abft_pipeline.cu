@@ -163,8 +163,13 @@ int enqueue_loop(abft_session* s, const abft_online_args* a, const std::vector<P
 int make_plan(abft_session* s, const abft_online_args* a, std::vector<Plan>& plan) {
     plan.assign(a->repeats, Plan{-1, -1, -1, -1});
     for (int it = 0; it < a->repeats; ++it) {
-        RC(abft_injection_plan(a->base_seed, a->rank, it, s->F, s->M_b, s->counts.data(), a->mode, a->zone_lo,
-                               a->zone_hi, &plan[it].frag, &plan[it].row, &plan[it].col, &plan[it].bit));
+        if (a->seed_scheme == ABFT_SEED_TILE)
+            RC(abft_injection_plan_tile(a->base_seed + (uint64_t)it, s->M_b, s->F, s->counts.data(), s->offsets.data(),
+                                        a->mode, a->zone_lo, a->zone_hi, &plan[it].frag, &plan[it].row,
+                                        &plan[it].col, &plan[it].bit));
+        else
+            RC(abft_injection_plan(a->base_seed, a->rank, it, s->F, s->M_b, s->counts.data(), a->mode, a->zone_lo,
+                                   a->zone_hi, &plan[it].frag, &plan[it].row, &plan[it].col, &plan[it].bit));
     }
     return ABFT_OK;
 }
@@ -230,6 +235,10 @@ int check_args(abft_session* s, const abft_online_args* a) {
     }
     if (a->correct_mode == ABFT_CORRECT_DRAIN && a->mode != ABFT_INJECT_NONE && a->repeats > s->max_iters) {
         set_error("online: drain correction needs repeats <= max_iters");
+        return ABFT_ERR_ARG;
+    }
+    if (a->seed_scheme != ABFT_SEED_REFERENCE && a->seed_scheme != ABFT_SEED_TILE) {
+        set_error("online: unknown seed scheme");
         return ABFT_ERR_ARG;
     }
     if (a->graph && a->repeats > s->max_iters) {

@@ -120,6 +120,17 @@ def swifi_zone_range(zone):
 MODES = {"none": INJECT_NONE, "add": INJECT_ADD, "swifi": INJECT_SWIFI}
 
 
+def injection_plan_tile(seed, M_b, counts, offsets, mode, zone="any"):
+    """Tile-uniform scheme: (frag, row, col, bit) from mt19937_64(seed), j uniform over the tile."""
+    counts = np.ascontiguousarray(counts, np.int32)
+    offsets = np.ascontiguousarray(offsets, np.int32)
+    lo, hi = swifi_zone_range(zone)
+    r = [ctypes.c_int() for _ in range(4)]
+    call("abft_injection_plan_tile", int(seed), int(M_b), len(counts), _iptr(counts), _iptr(offsets),
+         MODES[mode] if isinstance(mode, str) else int(mode), lo, hi, *[ctypes.byref(x) for x in r])
+    return tuple(x.value for x in r)
+
+
 def injection_plan(base_seed, rank, it, counts, M_b, mode, zone="any"):
     """(frag, row, col, bit) injected at iteration `it` (-1s when nothing is injected)."""
     counts = np.ascontiguousarray(counts, np.int32)

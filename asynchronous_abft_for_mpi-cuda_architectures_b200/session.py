@@ -95,7 +95,8 @@ class OnlineSession:
                  ctypes.byref(hms))
         return dms.value, hms.value
 
-    def _args(self, mode, zone, add_delta, base_seed, rank, repeats, correct, log, profile=False, graph=False):
+    def _args(self, mode, zone, add_delta, base_seed, rank, repeats, correct, log, profile=False, graph=False,
+              seed_scheme="reference"):
         lo, hi = host.swifi_zone_range(zone)
         a = OnlineArgs()
         a.mode = host.MODES[mode] if isinstance(mode, str) else int(mode)
@@ -108,6 +109,7 @@ class OnlineSession:
         a.log = int(bool(log))
         a.profile = int(bool(profile))
         a.graph = int(bool(graph))
+        a.seed_scheme = 1 if seed_scheme == "tile" else 0
         return a
 
     @staticmethod
@@ -117,7 +119,7 @@ class OnlineSession:
                     verify_ms_sum=r.verify_ms_sum, verify_ms_max=r.verify_ms_max)
 
     def online(self, mode="none", zone="any", add_delta=ADD_FAULT_DELTA, base_seed=0, rank=0, repeats=1,
-               correct="inloop", log=False, profile=False, graph=False):
+               correct="inloop", log=False, profile=False, graph=False, seed_scheme="reference"):
         """repeats protected iterations; returns timings, confusion matrix and restore count.
 
         profile=True brackets every verify launch with CUDA events on the verify
@@ -126,7 +128,7 @@ class OnlineSession:
         """
         if self.tau is None:
             raise RuntimeError("set_tau() first")
-        a = self._args(mode, zone, add_delta, base_seed, rank, repeats, correct, log, profile, graph)
+        a = self._args(mode, zone, add_delta, base_seed, rank, repeats, correct, log, profile, graph, seed_scheme)
         r = OnlineResult()
         with torch.cuda.device(self.device):
             call("abft_session_online", self.handle, ctypes.byref(a), ctypes.byref(r))

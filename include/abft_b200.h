@@ -37,6 +37,9 @@ extern "C" {
 #define ABFT_INJECT_ADD 1
 #define ABFT_INJECT_SWIFI 2
 
+#define ABFT_SEED_REFERENCE 0 /* injection draws of the reference (per rank, per iteration) */
+#define ABFT_SEED_TILE 1      /* abft_injection_plan_tile with seed = base_seed + iteration  */
+
 #define ABFT_CORRECT_INLOOP 0 /* correct inside the loop (reference behaviour) */
 #define ABFT_CORRECT_DRAIN 1  /* locate in the loop, correct after it          */
 
@@ -76,6 +79,13 @@ int abft_swifi_zone_range(const char* zone, int* lo, int* hi);
  * :91-98). mode ABFT_INJECT_*; outputs -1 when nothing is injected. */
 int abft_injection_plan(uint64_t base_seed, int rank, int it, int F, int M_b, const int* counts, int mode,
                         int zone_lo, int zone_hi, int* frag, int* row, int* col, int* bit);
+/* Tile-uniform injection scheme (no counterpart in the reference, whose
+ * injector cannot express it; the 1024^3 workload describes faults this way):
+ * mt19937_64(seed) draws row uniform over [0, M_b) and column j uniform over
+ * the whole tile [0, N_b), then the bit in [zone_lo, zone_hi] for SWIFI; the
+ * fragment is the one holding j and col = j - offsets[frag]. */
+int abft_injection_plan_tile(uint64_t seed, int M_b, int F, const int* counts, const int* offsets, int mode,
+                             int zone_lo, int zone_hi, int* frag, int* row, int* col, int* bit);
 
 /* ------------------------------------------------------------------------
  * Workspace: the device-side state of pipeline/buffers.cuh:7-46
@@ -220,6 +230,7 @@ typedef struct abft_online_args {
                          replayed; the injection plan goes to a device table
                          and the verify kernel applies the fault. Needs
                          repeats <= max_iters; ignores profile.            */
+    int seed_scheme;  /* ABFT_SEED_REFERENCE (default) or ABFT_SEED_TILE    */
 } abft_online_args;
 
 typedef struct abft_online_result {

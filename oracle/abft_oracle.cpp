@@ -294,6 +294,30 @@ void oracle_inject_position(uint64_t inject_seed, int frag, int M_b, int N_f, in
     }
 }
 
+// Tile-uniform scheme (the 1024^3 workload's wording, an extension the
+// reference cannot express): mt19937_64(seed) draws i uniform over the M_b
+// rows and j uniform over the whole N_b-column tile (then the bit when
+// lo <= hi); the fragment is the one that holds column j.
+void oracle_inject_position_tile(uint64_t seed, int M_b, int F, const int* counts, const int* offsets, int lo,
+                                 int hi, int* frag, int* row, int* col, int* bit) {
+    int N_b = 0;
+    for (int f = 0; f < F; ++f) N_b = std::max(N_b, offsets[f] + counts[f]);
+    std::mt19937_64 gen(seed);
+    std::uniform_int_distribution<int> rd(0, M_b - 1);
+    std::uniform_int_distribution<int> cd(0, N_b - 1);
+    *row = rd(gen);
+    const int j = cd(gen);
+    *bit = -1;
+    if (lo <= hi) {
+        std::uniform_int_distribution<int> bd(lo, hi);
+        *bit = bd(gen);
+    }
+    *frag = 0;
+    for (int f = 0; f < F; ++f)
+        if (j >= offsets[f] && j < offsets[f] + counts[f]) *frag = f;
+    *col = j - offsets[*frag];
+}
+
 // kernels/swifi.cuh:55-59 and :33-40
 void oracle_inject_add(float* C, i64 ldc, int row, int col, float delta) { C[(i64)row * ldc + col] += delta; }
 void oracle_inject_bitflip(float* C, i64 ldc, int row, int col, int bit) {
@@ -374,7 +398,7 @@ void oracle_online_loop(const float* C_clean, const float* A, const float* B, in
                         const int* counts, const int* offsets, const double* tau, int mode, int zone_lo,
                         int zone_hi, float add_delta, uint64_t base_seed, int rank, int repeats,
                         const float* golden, float* buf0, float* buf1, int* cm, int* n_restored, int* inj,
-                        int* errcol, int* errrow, double* rowdiff) {
+                        int* errcol, int* errrow, double* rowdiff, int seed_scheme) {
     const i64 tile = (i64)M_b * N_b;
     std::vector<double> colSumA(K), expRow(N_b), rowSumB((i64)F * K), expCol((i64)F * M_b);
     oracle_encode(A, K, B, N_b, M_b, K, F, counts, offsets, colSumA.data(), expRow.data(), rowSumB.data(),
@@ -386,7 +410,12 @@ void oracle_online_loop(const float* C_clean, const float* A, const float* B, in
         std::memcpy(C, C_clean, sizeof(float) * tile);
         int frag = -1, row = -1, col = -1, bit = -1;
         uint64_t seed = oracle_inject_seed(base_seed, rank, it);
-        if (inject_on) {
+        if (inject_on && seed_scheme == 1) {
+            oracle_inject_position_tile(base_seed + (uint64_t)it, M_b, F, counts, offsets, mode == 2 ? zone_lo : 1,
+                                        mode == 2 ? zone_hi : 0, &frag, &row, &col, &bit);
+            if (mode == 1) oracle_inject_add(C + offsets[frag], N_b, row, col, add_delta);
+            else oracle_inject_bitflip(C + offsets[frag], N_b, row, col, bit);
+        } else if (inject_on) {
             frag = oracle_inject_frag(seed, F);
             if (mode == 1) {
                 oracle_inject_position(seed, frag, M_b, counts[frag], 1, 0, &row, &col, &bit);

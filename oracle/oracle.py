@@ -44,13 +44,14 @@ _SIGS = {
     "oracle_inject_seed": (_U64, [_U64, _I, _I]),
     "oracle_inject_frag": (_I, [_U64, _I]),
     "oracle_inject_position": (None, [_U64, _I, _I, _I, _I, _I, _P, _P, _P]),
+    "oracle_inject_position_tile": (None, [_U64, _I, _I, _P, _P, _I, _I, _P, _P, _P, _P]),
     "oracle_inject_add": (None, [_P, _L, _I, _I, _F]),
     "oracle_inject_bitflip": (None, [_P, _L, _I, _I, _I]),
     "oracle_encode": (None, [_P, _L, _P, _L, _I, _I, _I, _P, _P, _P, _P, _P, _P]),
     "oracle_verify_iteration": (None, [_P, _L, _P, _L, _P, _L, _I, _I, _I, _P, _P, _P, _P, _P, _I, _I,
                                        _P, _L, _P, _P, _P, _P, _P]),
     "oracle_online_loop": (None, [_P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _I, _I, _I, _F, _U64, _I, _I,
-                                  _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+                                  _P, _P, _P, _P, _P, _P, _P, _P, _P, _I]),
 }
 
 
@@ -226,6 +227,15 @@ def inject_position(seed, frag, M_b, N_f, lo=1, hi=0):
     return r.value, c.value, b.value
 
 
+def inject_position_tile(seed, M_b, counts, offsets, lo=1, hi=0):
+    counts = _c(counts, np.int32)
+    offsets = _c(offsets, np.int32)
+    f, r, c, b = _I(), _I(), _I(), _I()
+    lib().oracle_inject_position_tile(int(seed), int(M_b), len(counts), _p(counts), _p(offsets), int(lo), int(hi),
+                                      ctypes.byref(f), ctypes.byref(r), ctypes.byref(c), ctypes.byref(b))
+    return f.value, r.value, c.value, b.value
+
+
 def verify_iteration(C, A, B, counts, offsets, expRow, tau, inject_frag=-1, do_localize=True, expCol=None,
                      golden=None):
     """Verify half of one online iteration on a rank tile C (modified in place).
@@ -259,7 +269,7 @@ MODES = {"none": 0, "add": 1, "swifi": 2}
 
 
 def online_loop(C_clean, A, B, counts, offsets, tau, mode="none", zone="any", add_delta=1.0e6, base_seed=0,
-                rank=0, repeats=1, golden=None):
+                rank=0, repeats=1, golden=None, seed_scheme="reference"):
     """Decision path of the reference's online loop for one rank, on the CPU."""
     C_clean = _c(C_clean, np.float32)
     A = _c(A, np.float32)
@@ -282,5 +292,6 @@ def online_loop(C_clean, A, B, counts, offsets, tau, mode="none", zone="any", ad
     golden = _c(golden, np.float32) if golden is not None else None
     lib().oracle_online_loop(_p(C_clean), _p(A), _p(B), M_b, K, N_b, F, _p(counts), _p(offsets), _p(tau),
                              MODES[mode], lo, hi, float(add_delta), int(base_seed), int(rank), int(repeats),
-                             _p(golden), _p(buf0), _p(buf1), _p(cm), _p(nr), _p(inj), _p(ec), _p(er), _p(rd))
+                             _p(golden), _p(buf0), _p(buf1), _p(cm), _p(nr), _p(inj), _p(ec), _p(er), _p(rd),
+                             1 if seed_scheme == "tile" else 0)
     return dict(buf0=buf0, buf1=buf1, cm=cm, n_restored=int(nr[0]), inj=inj, errcol=ec, errrow=er, rowdiff=rd)

@@ -61,3 +61,17 @@ def test_frag_policy(abft):
     assert abft.frag_count(1024, 1024, 1024, 1024, 1024, 4) == 4
     assert abft.frag_count(4096, 4096, 4096, 4096, 4096, 4, frag_cap=1 << 20) == 16
     assert abft.frag_count(4096, 4096, 4096, 4096, 3, 4) == 3          # never more than N_b
+
+
+def test_tile_injection_scheme_matches_oracle(abft, orc):
+    """The tile-uniform scheme (seed 1 + iteration, (i, j) uniform over the tile)."""
+    counts, offsets = abft.split_dim(1030, 3)
+    for seed in range(1, 40):
+        for mode, zone in (("add", "any"), ("swifi", "any"), ("swifi", "exponent")):
+            got = abft.host.injection_plan_tile(seed, 777, counts, offsets, mode, zone)
+            lo, hi = (1, 0) if mode == "add" else orc.swifi_zone_range(zone)
+            want = orc.inject_position_tile(seed, 777, counts, offsets, lo, hi)
+            assert got == want
+            f, r, c, b = got
+            assert 0 <= r < 777 and 0 <= c < counts[f]
+    assert abft.host.injection_plan_tile(5, 10, counts, offsets, "none") == (-1, -1, -1, -1)

@@ -160,3 +160,16 @@ def test_graph_mode_uneven_and_small_fragments(abft, orc):
     with pytest.raises(abft.AbftError):
         s.online("add", repeats=10, graph=True)  # beyond the plan table
     s.close()
+
+
+@pytest.mark.parametrize("graph", [False, True])
+def test_tile_seed_scheme(graph, abft, orc):
+    """1024^3 with +1.0 faults at (i, j) uniform over the tile from seed 1 + iteration."""
+    s, A, B, counts, offsets, tau, C0 = make_session(abft, orc, 1024, 1024, 1024, 4, 0, 0, max_iters=10)
+    s.set_golden(torch.from_numpy(C0).cuda())
+    res = s.online("add", add_delta=1.0, base_seed=1, repeats=10, log=True, graph=graph, seed_scheme="tile")
+    o = orc.online_loop(C0, A, B, counts, offsets, tau, "add", "any", 1.0, 1, 0, 10, golden=C0,
+                        seed_scheme="tile")
+    compare(s, res, o, 10)
+    assert res["cm"][0] == 10 and res["n_restored"] == 10
+    s.close()
