@@ -29,8 +29,10 @@
 #include <stdint.h>
 
 #include <algorithm>
+#include <map>
 #include <mutex>
 #include <set>
+#include <tuple>
 #include <string>
 
 #include "abft_b200.h"
@@ -730,10 +732,12 @@ int check_launch(const char* what) {
 }
 
 // Verify geometry: column groups x row chunks, about two CTAs per SM.
-void verify_geometry(int sms, int M, int N, int& groups, int& chunks, int& rows_per) {
+// Verify geometry: column groups x row chunks, sized to one full wave of
+// resident CTAs (target = resident CTAs per SM x SMs; a second, mostly empty
+// wave would double the launch time).
+void verify_geometry(int target, int M, int N, int& groups, int& chunks, int& rows_per) {
     groups = (N + kGroupCols - 1) / kGroupCols;
-    int target = 4 * sms;
-    chunks = (target + groups - 1) / groups;
+    chunks = target / groups;
     if (chunks < 1) chunks = 1;
     if (chunks > kMaxChunks) chunks = kMaxChunks;
     rows_per = (M + chunks - 1) / chunks;
@@ -741,6 +745,25 @@ void verify_geometry(int sms, int M, int N, int& groups, int& chunks, int& rows_
     // at least one full batch per warp: bounds the atomics per accumulator to M / 64
     rows_per = std::max(rows_per, kBatch * kWarps);
     chunks = (M + rows_per - 1) / rows_per;
+}
+
+// Resident CTAs per SM of a kernel at a dynamic shared memory size (cached).
+int resident_per_sm(const void* fn, int smem) {
+    static std::mutex mu;
+    static std::map<std::tuple<int, const void*, int>, int> cache;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    auto key = std::make_tuple(dev, fn, smem);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, kThreads, smem) != cudaSuccess || n < 1) {
+        (void)cudaGetLastError();
+        n = 1;
+    }
+    cache[key] = n;
+    return n;
 }
 
 }  // namespace
@@ -815,15 +838,18 @@ int launch_verify(abft_ws* ws, const float* dC, int64_t ldc, int f, double tau, 
     const int M = ws->M_b, N = ws->counts[f];
     const float* Cf = dC + ws->offsets[f];
     if (int rc = ensure_kernel_attrs(ws->device)) return rc;
-    int groups, chunks, rows_per;
-    verify_geometry(ws->sms, M, N, groups, chunks, rows_per);
     const bool vec = aligned16(Cf) && (ldc % 4 == 0) && (N % 4 == 0);
+    // d / w of the last CTA live in the 16 KB reduction area when they fit,
+    // otherwise in the workspace: every CTA keeps a small shared footprint.
+    const int reduce_bytes = kWarps * kGroupCols * 16;
+    const int dw_in_smem = (16LL * N <= reduce_bytes) ? 1 : 0;
+    const int smem = reduce_bytes;
+    const int per_sm = resident_per_sm(vec ? (const void*)k_verify<true> : (const void*)k_verify<false>, smem);
+    int groups, chunks, rows_per;
+    verify_geometry(per_sm * ws->sms, M, N, groups, chunks, rows_per);
     dim3 grid(groups, chunks);
     const double* expv = ws->d.expRow + ws->offsets[f];
     if (it >= ws->max_iters) it = -1;
-    const int reduce_bytes = kWarps * kGroupCols * 16;
-    const int dw_in_smem = (16LL * N <= kVerifySmemMax) ? 1 : 0;
-    const int smem = dw_in_smem ? std::max(reduce_bytes, 16 * N) : reduce_bytes;
     const int total = groups * chunks;
     const InjectPlan* plan = (plan_it >= 0) ? ws->d.plan : nullptr;
     float* Cw = const_cast<float*>(Cf);
@@ -976,11 +1002,12 @@ int launch_verify_static(const float* Cf, int64_t ldc, int M, int N, const doubl
     w.vcnt = reinterpret_cast<int*>(s.base + kStaticColBytes);
     w.rec = reinterpret_cast<FragRecord*>(s.base + kStaticColBytes + 256);
     w.ctr = reinterpret_cast<Counters*>(s.base + kStaticColBytes + 512);
-    int groups, chunks, rows_per;
-    verify_geometry(s.sms, M, N, groups, chunks, rows_per);
     const bool vec = aligned16(Cf) && (ldc % 4 == 0) && (N % 4 == 0);
     const int reduce_bytes = kWarps * kGroupCols * 16;
     const int smem = std::max(reduce_bytes, 16 * N);  // d / w always fit: N <= kStaticMaxCols
+    const int per_sm = resident_per_sm(vec ? (const void*)k_verify<true> : (const void*)k_verify<false>, smem);
+    int groups, chunks, rows_per;
+    verify_geometry(per_sm * s.sms, M, N, groups, chunks, rows_per);
     dim3 grid(groups, chunks);
     const int total = groups * chunks;
     if (vec)
