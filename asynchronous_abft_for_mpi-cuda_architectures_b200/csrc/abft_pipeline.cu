@@ -59,6 +59,11 @@ struct abft_session {
     InjectPlan* plan_host = nullptr;  // pinned, max_iters entries
     cudaGraphExec_t bexec = nullptr;  // graph of the baseline pass
     int b_repeats = -1;
+    // run_host: copy stream, input arrivals (A, then B per fragment), final
+    // fragments ready for the host
+    cudaStream_t xfer = nullptr;
+    cudaEvent_t a_in = nullptr, xjoin = nullptr;
+    std::vector<cudaEvent_t> b_in, c_out;
 };
 
 namespace {
@@ -104,11 +109,21 @@ struct Plan {
     int frag, row, col, bit;
 };
 
+// Transfer points of run_host: iteration 0's SGEMM of fragment f waits for A
+// and for B's fragment f to arrive; the last iteration's fragment f records
+// out_ready[f] once its verification and correction are enqueued, so that its
+// copy to the host overlaps the SGEMMs of the fragments after it.
+struct IoHooks {
+    cudaEvent_t a_ready;
+    const cudaEvent_t* b_ready;
+    const cudaEvent_t* out_ready;  // null: no per-fragment signal
+};
+
 // Enqueue `repeats` protected iterations on the two streams (no host sync).
 // graph = true: the injection is read from the device plan table by the verify
 // kernel (capturable, the same graph serves every trial).
 int enqueue_loop(abft_session* s, const abft_online_args* a, const std::vector<Plan>& plan, int* launches,
-                 int* vlaunches, bool graph = false) {
+                 int* vlaunches, bool graph = false, const IoHooks* io = nullptr) {
     const bool inject_on = (a->mode == ABFT_INJECT_ADD || a->mode == ABFT_INJECT_SWIFI);
     const bool do_localize = inject_on;
     bool used[2] = {false, false};
@@ -119,6 +134,10 @@ int enqueue_loop(abft_session* s, const abft_online_args* a, const std::vector<P
         if (used[bi]) CK(cudaStreamWaitEvent(s->compute, s->buf_done[bi], 0));
         const int log_it = (a->log && it < s->max_iters) ? it : -1;
         for (int f = 0; f < s->F; ++f) {
+            if (io && it == 0) {
+                if (f == 0) CK(cudaStreamWaitEvent(s->compute, io->a_ready, 0));
+                CK(cudaStreamWaitEvent(s->compute, io->b_ready[f], 0));
+            }
             RC(sgemm_frag(s, dC, f));
             if (!graph && f == plan[it].frag) {
                 InjectLog* lg = (log_it >= 0) ? s->ws->d.ilog + log_it : nullptr;
@@ -147,6 +166,7 @@ int enqueue_loop(abft_session* s, const abft_online_args* a, const std::vector<P
                                    s->verify, graph ? it : -1));
                 ++nl;
             }
+            if (io && io->out_ready && it == a->repeats - 1) CK(cudaEventRecord(io->out_ready[f], s->verify));
         }
         CK(cudaEventRecord(s->buf_done[bi], s->verify));
         used[bi] = true;
@@ -332,6 +352,15 @@ int abft_session_create(const abft_session_cfg* c, abft_session** out) {
     if (e == cudaSuccess) e = cudaEventCreate(&s->t1);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s->vjoin, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s->cjoin, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s->a_in, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s->xjoin, cudaEventDisableTiming);
+    s->b_in.assign(s->F, nullptr);
+    s->c_out.assign(s->F, nullptr);
+    for (int f = 0; f < s->F && e == cudaSuccess; ++f) {
+        e = cudaEventCreateWithFlags(&s->b_in[f], cudaEventDisableTiming);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s->c_out[f], cudaEventDisableTiming);
+    }
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&s->xfer, cudaStreamNonBlocking);
     if (e != cudaSuccess) return fail(cuda_fail(e, "event create"));
     int rc = abft_ws_create(s->M_b, s->N_b, s->K, s->F, c->counts, c->offsets, c->max_iters, nullptr, 0, &s->ws);
     if (rc != ABFT_OK) return fail(rc);
@@ -347,6 +376,7 @@ int abft_session_destroy(abft_session* s) {
     if (!s) return ABFT_OK;
     if (s->compute) cudaStreamSynchronize(s->compute);
     if (s->verify) cudaStreamSynchronize(s->verify);
+    if (s->xfer) cudaStreamSynchronize(s->xfer);
     drop_graph(s);
     if (s->bexec) cudaGraphExecDestroy(s->bexec);
     if (s->plan_host) cudaFreeHost(s->plan_host);
@@ -354,8 +384,13 @@ int abft_session_destroy(abft_session* s) {
         if (e) cudaEventDestroy(e);
     for (auto e : s->vprof)
         if (e) cudaEventDestroy(e);
-    for (auto e : {s->buf_done[0], s->buf_done[1], s->t0, s->t1, s->vjoin, s->cjoin})
+    for (auto e : {s->buf_done[0], s->buf_done[1], s->t0, s->t1, s->vjoin, s->cjoin, s->a_in, s->xjoin})
         if (e) cudaEventDestroy(e);
+    for (auto e : s->b_in)
+        if (e) cudaEventDestroy(e);
+    for (auto e : s->c_out)
+        if (e) cudaEventDestroy(e);
+    if (s->xfer) cudaStreamDestroy(s->xfer);
     if (s->handle) cublasDestroy(s->handle);
     if (s->compute) cudaStreamDestroy(s->compute);
     if (s->verify) cudaStreamDestroy(s->verify);
@@ -547,27 +582,47 @@ int abft_session_run_host(abft_session* s, const float* hA, const float* hB, flo
     CK(cudaStreamSynchronize(s->compute));
     const auto h0 = std::chrono::high_resolution_clock::now();
     CK(cudaEventRecord(s->t0, s->compute));
-    // inputs: host -> device (row-major stripes, possibly padded)
+    CK(cudaStreamWaitEvent(s->xfer, s->t0, 0));
+    // inputs: host -> device on the copy stream, A first, then B one fragment
+    // (column block) at a time; iteration 0's SGEMM of fragment f starts as
+    // soon as A and B's fragment f are in.
     CK(cudaMemcpy2DAsync(const_cast<float*>(s->dA), sizeof(float) * s->lda, hA, sizeof(float) * s->K,
-                         sizeof(float) * s->K, s->M_b, cudaMemcpyHostToDevice, s->compute));
-    CK(cudaMemcpy2DAsync(const_cast<float*>(s->dB), sizeof(float) * s->ldb, hB, sizeof(float) * s->N_b,
-                         sizeof(float) * s->N_b, s->K, cudaMemcpyHostToDevice, s->compute));
-    CK(cudaEventRecord(s->cjoin, s->compute));
-    CK(cudaStreamWaitEvent(s->verify, s->cjoin, 0));
+                         sizeof(float) * s->K, s->M_b, cudaMemcpyHostToDevice, s->xfer));
+    CK(cudaEventRecord(s->a_in, s->xfer));
+    for (int f = 0; f < s->F; ++f) {
+        const int off = s->offsets[f];
+        CK(cudaMemcpy2DAsync(const_cast<float*>(s->dB) + off, sizeof(float) * s->ldb, hB + off,
+                             sizeof(float) * s->N_b, sizeof(float) * s->counts[f], s->K, cudaMemcpyHostToDevice,
+                             s->xfer));
+        CK(cudaEventRecord(s->b_in[f], s->xfer));
+    }
+    // the checksums need all of B: encoded on the verify stream while the
+    // first SGEMMs run
+    CK(cudaStreamWaitEvent(s->verify, s->b_in[s->F - 1], 0));
     int nl = 0, nv = 0;
     RC(abft_ws_reset_counters(s->ws, s->verify));
     RC(launch_encode(s->ws, s->dA, s->lda, s->dB, s->ldb, s->verify, &nl));
     s->encoded = true;
-    CK(cudaEventRecord(s->vjoin, s->verify));
-    CK(cudaStreamWaitEvent(s->compute, s->vjoin, 0));
+    // result: device -> host. With in-loop correction each fragment of the
+    // final buffer is final once its last verification and correction ran,
+    // and is copied then; drain correction rewrites the buffer after the loop.
+    const bool drain = (a->mode == ABFT_INJECT_ADD || a->mode == ABFT_INJECT_SWIFI) &&
+                       a->correct_mode == ABFT_CORRECT_DRAIN;
+    const IoHooks io{s->a_in, s->b_in.data(), drain ? nullptr : s->c_out.data()};
     int nl2 = 0;
-    RC(enqueue_loop(s, a, plan, &nl2, &nv));
+    RC(enqueue_loop(s, a, plan, &nl2, &nv, false, &io));
     CK(cudaEventRecord(s->vjoin, s->verify));
-    CK(cudaStreamWaitEvent(s->compute, s->vjoin, 0));
-    // result: device -> host (final buffer of the loop, and the counters)
     const float* last = s->dC[(a->repeats - 1) & 1];
-    CK(cudaMemcpy2DAsync(hC, sizeof(float) * s->N_b, last, sizeof(float) * s->ldc, sizeof(float) * s->N_b, s->M_b,
-                         cudaMemcpyDeviceToHost, s->compute));
+    if (drain) CK(cudaStreamWaitEvent(s->xfer, s->vjoin, 0));
+    for (int f = 0; f < s->F; ++f) {
+        const int off = s->offsets[f];
+        if (!drain) CK(cudaStreamWaitEvent(s->xfer, s->c_out[f], 0));
+        CK(cudaMemcpy2DAsync(hC + off, sizeof(float) * s->N_b, last + off, sizeof(float) * s->ldc,
+                             sizeof(float) * s->counts[f], s->M_b, cudaMemcpyDeviceToHost, s->xfer));
+    }
+    CK(cudaEventRecord(s->xjoin, s->xfer));
+    CK(cudaStreamWaitEvent(s->compute, s->vjoin, 0));
+    CK(cudaStreamWaitEvent(s->compute, s->xjoin, 0));
     Counters hc{};
     CK(cudaMemcpyAsync(&hc, s->ws->d.ctr, sizeof(hc), cudaMemcpyDeviceToHost, s->compute));
     CK(cudaEventRecord(s->t1, s->compute));

@@ -266,7 +266,12 @@ int abft_session_read_injections(abft_session* s, int it_count, int* inj4, float
 /* End-to-end call from HOST memory: copies hA, hB into the session's A and B
  * (which must be device buffers it may overwrite), encodes, runs `repeats`
  * protected iterations and copies the final C buffer and the counters back.
- * Timed with CUDA events around the copies (e2e_ms). */
+ * The copies overlap the work: B arrives one fragment at a time and
+ * iteration 0's SGEMM of a fragment starts once A and that fragment are in;
+ * with in-loop correction each fragment of the final buffer goes back to the
+ * host as soon as its last check finished. Always enqueued eagerly
+ * (args->graph is ignored). Timed with CUDA events around the copies
+ * (e2e_ms). hA, hB, hC should be pinned for the copies to be asynchronous. */
 int abft_session_run_host(abft_session* s, const float* hA, const float* hB, float* hC,
                           const abft_online_args* args, abft_online_result* res, double* e2e_ms);
 

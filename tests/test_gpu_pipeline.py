@@ -133,6 +133,34 @@ def test_baseline_and_run_host(abft, orc):
     s.close()
 
 
+@pytest.mark.parametrize("mode,correct,repeats", [("swifi", "inloop", 5), ("swifi", "drain", 5), ("add", "inloop", 4),
+                                                  ("none", "inloop", 1)])
+def test_run_host_overlapped_copies(mode, correct, repeats, abft, orc):
+    """run_host uploads B one fragment at a time and (in-loop correction)
+    downloads each final fragment as soon as it is checked: uneven fragments,
+    every element of the host output written, repeated calls stay exact."""
+    M, K, N, F = 1100, 300, 1030, 3
+    s, A, B, counts, offsets, tau, C0 = make_session(abft, orc, M, K, N, F, 5, 7, max_iters=8)
+    golden = C0 if mode == "swifi" else None
+    s.set_golden(torch.from_numpy(C0).cuda() if golden is not None else None)
+    hA = torch.from_numpy(A).pin_memory()
+    hB = torch.from_numpy(B).pin_memory()
+    for trial in range(2):
+        base = 41 + trial * 31337
+        s.A.zero_()
+        s.B.zero_()
+        torch.cuda.synchronize()
+        hC = torch.full((M, N), float("nan"), dtype=torch.float32).pin_memory()
+        res = s.run_host(hA, hB, hC, mode, base_seed=base, rank=1, repeats=repeats, correct=correct)
+        # drain correction ends with the same buffers as in-loop correction
+        o = orc.online_loop(C0, A, B, counts, offsets, tau, mode, "any", 1.0e6, base, 1, repeats, golden=golden)
+        assert res["cm"] == list(o["cm"])
+        assert res["n_restored"] == o["n_restored"]
+        want = o["buf0"] if (repeats - 1) % 2 == 0 else o["buf1"]
+        assert np.array_equal(hC.numpy().view(np.uint32), want.view(np.uint32))
+    s.close()
+
+
 @pytest.mark.parametrize("mode,zone,correct", [("swifi", "any", "inloop"), ("add", "any", "inloop"),
                                                 ("none", "any", "inloop"), ("swifi", "exponent", "drain")])
 def test_graph_mode_matches_oracle(mode, zone, correct, abft, orc):
