@@ -7,16 +7,30 @@ torch.distributed (NCCL) plumbing for multi-GPU runs. Importing it without the
 built library raises ImportError; there is no CPU fallback.
 """
 from ._lib import (ADD_FAULT_DELTA, CORRECT_DRAIN, CORRECT_INLOOP, DRIVER_PATH, HEADER_PATH, INJECT_ADD,
-                   INJECT_NONE, INJECT_SWIFI, LIB_PATH, SIGNATURES, AbftError, lib)
-from . import host
+                   INJECT_NONE, INJECT_SWIFI, LIB_PATH, SIGNATURES, AbftError, call, lib)
+from . import _lib, host
 from .host import (choose_grid, fill_random, frag_count, frag_thresholds, injection_plan, rank_tile,
                    relative_threshold, split_dim, swifi_zone_range, threshold_formula)
+
+
+VERIFY_KERNELS = {"auto": 0, "ldg": 1, "tma": 2}
+
+
+def set_verify_kernel(which):
+    """Verify body for every later verify launch in this process: "auto" (by
+    fragment size), "ldg" (128-bit loads) or "tma" (bulk tensor copies through
+    shared memory). Returns the previous setting."""
+    prev = lib.abft_set_verify_kernel(VERIFY_KERNELS[which])
+    if prev < 0:
+        raise AbftError("abft_set_verify_kernel", prev, _lib.last_error())
+    return {v: k for k, v in VERIFY_KERNELS.items()}[prev]
+
 
 __all__ = [
     "ADD_FAULT_DELTA", "CORRECT_DRAIN", "CORRECT_INLOOP", "DRIVER_PATH", "HEADER_PATH", "INJECT_ADD", "INJECT_NONE",
     "INJECT_SWIFI", "LIB_PATH", "SIGNATURES", "AbftError", "lib", "host", "choose_grid", "fill_random",
     "frag_count", "frag_thresholds", "injection_plan", "rank_tile", "relative_threshold", "split_dim",
-    "swifi_zone_range", "threshold_formula",
+    "swifi_zone_range", "threshold_formula", "call", "set_verify_kernel", "VERIFY_KERNELS",
 ]
 
 

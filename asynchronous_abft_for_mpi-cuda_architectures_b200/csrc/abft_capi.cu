@@ -214,6 +214,10 @@ int abft_ws_read_counters(abft_ws* ws, int cm[4], int* n_restored) {
     if (e != cudaSuccess) return cuda_fail(e, "read counters");
     for (int i = 0; i < 4; ++i) cm[i] = c.cm[i];
     if (n_restored) *n_restored = c.n_restored;
+    if (c.fault) {
+        set_error("verify: a bulk tensor copy did not complete within the wait limit; the decisions are void");
+        return ABFT_ERR_CUDA;
+    }
     return ABFT_OK;
 }
 
@@ -282,6 +286,15 @@ int abft_calibrate(abft_ws* ws, const float* dC, int64_t ldc, int f, double* dDi
         return ABFT_ERR_ARG;
     }
     return launch_verify(ws, dC, ldc, f, INFINITY, 0, -1, (cudaStream_t)stream, -1, 0.f, 0, dDiff);
+}
+
+int abft_set_verify_kernel(int which) {
+    const int prev = set_verify_kernel(which);
+    if (prev < 0) {
+        set_error("abft_set_verify_kernel: which must be ABFT_VERIFY_AUTO, _LDG or _TMA");
+        return ABFT_ERR_ARG;
+    }
+    return prev;
 }
 
 int abft_verify_noalloc(const float* dC_frag, int64_t ldc, int M, int N, const double* dExpRow, double tau,

@@ -51,7 +51,8 @@ struct Counters {
     int cm[4];       // TP, TN, FP, FN
     int n_restored;
     int n_pending;
-    int pad[2];
+    int fault;  // a verify kernel's bounded wait for a bulk copy ran out
+    int pad;
 };
 
 // Device-side workspace pointers (plain struct, passed by value to kernels).
@@ -121,6 +122,8 @@ int launch_drain(abft_ws* ws, float* dC0, float* dC1, int64_t ldc, const float* 
                  cudaStream_t st);
 int launch_inject(float* dC, int64_t ldc, int row, int col, int mode, float delta, int bit, InjectLog* log,
                   int frag, cudaStream_t st);
+// Selects the verify body (ABFT_VERIFY_*); returns the previous setting or -1.
+int set_verify_kernel(int which);
 int launch_verify_static(const float* Cf, int64_t ldc, int M, int N, const double* expv, double tau, int injected,
                          int* errcol, double* rowdiff, int* cm, cudaStream_t st);
 

@@ -24,11 +24,14 @@
 // shared memory by a deep cp.async pipeline so that the chain latency, not
 // memory latency, bounds them.
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdint.h>
 
 #include <algorithm>
+#include <atomic>
 #include <map>
 #include <mutex>
 #include <set>
@@ -44,6 +47,18 @@ namespace {
 constexpr unsigned kFull = 0xffffffffu;
 constexpr int kListCap = 256;
 constexpr int kBatch = 8;   // rows in flight per warp in the verify body
+// TMA-staged verify: 32-row x 128-column boxes (16 KB) through a 6-stage ring.
+constexpr int kTmaRows = 32;
+constexpr int kTmaStages = 6;
+constexpr int kStageBytes = kTmaRows * kGroupCols * 4;
+constexpr int kTmaSmem = kTmaStages * kStageBytes;
+// Fragments of at least this many bytes use the TMA body by default: measured on
+// B200 with L2 emptied before each launch, the two bodies are within 1 us of
+// each other up to 268 MB (128-bit loads ahead by 2-8 %), TMA ahead by 2 % at 1 GiB.
+constexpr long long kTmaMinBytes = 512LL << 20;
+// Bound of every mbarrier wait (try_wait polls); a wait that runs out records a
+// fault in the counters instead of spinning on.
+constexpr int kSpinLimit = 1 << 20;
 
 // ------------------------------------------------------------- helpers ----
 
@@ -54,6 +69,50 @@ __device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_re
 
 // Hint: bring the 128-byte line holding p into L2 (no register result, no fault).
 __device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];\n" ::"l"(p)); }
+
+// --- mbarrier + bulk tensor copy (TMA) primitives, shared::cta addresses ---
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+// Makes the initialised barriers visible to the async (TMA) proxy.
+__device__ __forceinline__ void mbar_init_fence() {
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait for the phase with the given parity to complete.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    for (int i = 0; i < kSpinLimit; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+
+// One 2-D box of the tensor map (x = column, y = row) into shared memory,
+// completing on bar. No multicast.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];\n" ::"r"(smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
+}
 
 // Window w >= 0 with |d_reference - d| <= w for a sum S of n float terms with
 // float |x|-sum T and smallest (|x| bits - 1) mbm1; w == 0 means S (and so d)
@@ -233,114 +292,23 @@ __device__ int final_select(int n, double tau, const double* __restrict__ expv, 
 
 // ------------------------------------------------------------- verify -----
 
-// Fused actualRow + detect for one fragment (M x N, leading dimension ldc).
-// grid = (groups of 128 columns, row chunks). Each CTA streams its tile with
-// 128-bit loads, reduces it to per-column (sum, |x|-sum, smallest |x|) and
-// adds those into per-column accumulators with device atomics (any order:
-// certified sums are exact in every order, uncertified ones carry a window
-// valid for every order). The last CTA to finish certifies each column and
-// runs the reference's arg-max. Shared memory: 16 KB for the CTA reduction,
-// reused by the last CTA for the d / w arrays when 16*N bytes fit.
-template <bool VEC>
-__global__ void __launch_bounds__(kThreads, 4)
-    k_verify(const float* __restrict__ C, long long ldc, int M, int N, int rows_per, int total_ctas, int dw_in_smem,
-             const double* __restrict__ expv, double tau, int injected, int f, int F, int it, WsDev w,
-             float* Cw, const InjectPlan* __restrict__ plan, int plan_it, float add_delta, int log_inj,
-             double* calib_out) {
-    extern __shared__ __align__(16) unsigned char dsm[];
-    __shared__ SelectSmem sel;
+// Second half of the verify kernels: fold the CTA's per-column partials
+// (S, |x|-sum, smallest |x| bits - 1 of columns c0..c0+3 in each thread) into
+// the per-column accumulators; the last CTA to arrive certifies every column
+// and runs the reference's arg-max (or writes the calibration differences).
+// dsm: at least kWarps * kGroupCols * 16 bytes of dynamic shared memory that
+// no copy writes any more.
+__device__ __forceinline__ void verify_tail(unsigned char* dsm, SelectSmem& sel, double s0, double s1, double s2,
+                                            double s3, float t0, float t1, float t2, float t3, uint32_t m0,
+                                            uint32_t m1, uint32_t m2, uint32_t m3, const float* __restrict__ C,
+                                            long long ldc, int M, int N, int total_ctas, int dw_in_smem,
+                                            const double* __restrict__ expv, double tau, int injected, int f, int F,
+                                            int it, const WsDev& w, double* calib_out) {
     double(*s_s)[kGroupCols] = reinterpret_cast<double(*)[kGroupCols]>(dsm);
     float(*s_t)[kGroupCols] = reinterpret_cast<float(*)[kGroupCols]>(dsm + kWarps * kGroupCols * 8);
     uint32_t(*s_m)[kGroupCols] = reinterpret_cast<uint32_t(*)[kGroupCols]>(dsm + kWarps * kGroupCols * 12);
-
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int g = blockIdx.x, chunk = blockIdx.y;
-    const int c0 = g * kGroupCols + lane * 4;
-    const int r0 = chunk * rows_per;
-    const int r1 = min(M, r0 + rows_per);
-
-    // The expected checksums of this group's columns (1 KB) are read only by
-    // the last CTA; the first row chunk pulls them into L2 meanwhile.
-    if (chunk == 0 && tid < kGroupCols / 16 && g * kGroupCols + tid * 16 < N)
-        prefetch_l2(expv + g * kGroupCols + tid * 16);
-
-    double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
-    float t0 = 0.f, t1 = 0.f, t2 = 0.f, t3 = 0.f;
-    uint32_t m0 = kFull, m1 = kFull, m2 = kFull, m3 = kFull;
-
-    // Graph mode: this iteration's planned fault is applied here, by the one
-    // thread whose loads cover the element (nothing reads C between the SGEMM
-    // and this kernel, so the result equals injecting on the compute stream).
-    int inj_row = -1, inj_k = 0, inj_bit = -1;
-    if (plan != nullptr) {
-        const InjectPlan p = plan[plan_it];
-        injected = (p.frag == f) ? 1 : 0;
-        if (injected && p.row >= r0 && p.row < r1 && ((p.row - r0) % kWarps) == warp && p.col >= c0 &&
-            p.col < c0 + 4 && p.col < N) {
-            inj_row = p.row;
-            inj_k = p.col - c0;
-            inj_bit = p.bit;
-        }
-    }
-
-    auto load = [&](int r) -> float4 {
-        const float* p = C + (long long)r * ldc + c0;
-        if (VEC) {
-            if (c0 < N) return __ldg(reinterpret_cast<const float4*>(p));
-            return make_float4(0.f, 0.f, 0.f, 0.f);
-        } else {
-            float4 v;
-            v.x = (c0 + 0 < N) ? __ldg(p + 0) : 0.f;
-            v.y = (c0 + 1 < N) ? __ldg(p + 1) : 0.f;
-            v.z = (c0 + 2 < N) ? __ldg(p + 2) : 0.f;
-            v.w = (c0 + 3 < N) ? __ldg(p + 3) : 0.f;
-            return v;
-        }
-    };
-    auto acc = [&](float4 v) {
-        acc1(v.x, s0, t0, m0);
-        acc1(v.y, s1, t1, m1);
-        acc1(v.z, s2, t2, m2);
-        acc1(v.w, s3, t3, m3);
-    };
-
-    // Batches of kBatch rows per warp, predicated, so that every load of a
-    // batch is in flight at once (one memory latency per batch).
-    for (int r = r0 + warp; r < r1; r += kBatch * kWarps) {
-        float4 v[kBatch];
-#pragma unroll
-        for (int u = 0; u < kBatch; ++u) {
-            const int rr = r + u * kWarps;
-            v[u] = (rr < r1) ? load(rr) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-        if (inj_row >= 0) {
-#pragma unroll
-            for (int u = 0; u < kBatch; ++u) {
-                if (r + u * kWarps == inj_row) {
-                    const float before = inj_k == 0 ? v[u].x : inj_k == 1 ? v[u].y : inj_k == 2 ? v[u].z : v[u].w;
-                    const float after = (inj_bit < 0) ? __fadd_rn(before, add_delta)
-                                                      : __uint_as_float(__float_as_uint(before) ^ (1u << inj_bit));
-                    if (inj_k == 0) v[u].x = after;
-                    else if (inj_k == 1) v[u].y = after;
-                    else if (inj_k == 2) v[u].z = after;
-                    else v[u].w = after;
-                    Cw[(long long)inj_row * ldc + c0 + inj_k] = after;
-                    if (log_inj) {
-                        InjectLog& L = w.ilog[plan_it];
-                        L.frag = f;
-                        L.row = inj_row;
-                        L.col = c0 + inj_k;
-                        L.bit = inj_bit;
-                        L.before = before;
-                        L.after = after;
-                    }
-                }
-            }
-        }
-#pragma unroll
-        for (int u = 0; u < kBatch; ++u) acc(v[u]);
-    }
-
+    const int g = blockIdx.x;
     const int cl = lane * 4;
     s_s[warp][cl + 0] = s0; s_s[warp][cl + 1] = s1; s_s[warp][cl + 2] = s2; s_s[warp][cl + 3] = s3;
     s_t[warp][cl + 0] = t0; s_t[warp][cl + 1] = t1; s_t[warp][cl + 2] = t2; s_t[warp][cl + 3] = t3;
@@ -439,6 +407,239 @@ __global__ void __launch_bounds__(kThreads, 4)
         }
         *w.vcnt = 0;
     }
+}
+
+
+// Fused actualRow + detect for one fragment (M x N, leading dimension ldc).
+// grid = (groups of 128 columns, row chunks). Each CTA streams its tile with
+// 128-bit loads, reduces it to per-column (sum, |x|-sum, smallest |x|) and
+// adds those into per-column accumulators with device atomics (any order:
+// certified sums are exact in every order, uncertified ones carry a window
+// valid for every order). The last CTA to finish certifies each column and
+// runs the reference's arg-max. Shared memory: 16 KB for the CTA reduction,
+// reused by the last CTA for the d / w arrays when 16*N bytes fit.
+template <bool VEC>
+__global__ void __launch_bounds__(kThreads, 4)
+    k_verify(const float* __restrict__ C, long long ldc, int M, int N, int rows_per, int total_ctas, int dw_in_smem,
+             const double* __restrict__ expv, double tau, int injected, int f, int F, int it, WsDev w,
+             float* Cw, const InjectPlan* __restrict__ plan, int plan_it, float add_delta, int log_inj,
+             double* calib_out) {
+    extern __shared__ __align__(16) unsigned char dsm[];
+    __shared__ SelectSmem sel;
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = blockIdx.x, chunk = blockIdx.y;
+    const int c0 = g * kGroupCols + lane * 4;
+    const int r0 = chunk * rows_per;
+    const int r1 = min(M, r0 + rows_per);
+
+    // The expected checksums of this group's columns (1 KB) are read only by
+    // the last CTA; the first row chunk pulls them into L2 meanwhile.
+    if (chunk == 0 && tid < kGroupCols / 16 && g * kGroupCols + tid * 16 < N)
+        prefetch_l2(expv + g * kGroupCols + tid * 16);
+
+    double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
+    float t0 = 0.f, t1 = 0.f, t2 = 0.f, t3 = 0.f;
+    uint32_t m0 = kFull, m1 = kFull, m2 = kFull, m3 = kFull;
+
+    // Graph mode: this iteration's planned fault is applied here, by the one
+    // thread whose loads cover the element (nothing reads C between the SGEMM
+    // and this kernel, so the result equals injecting on the compute stream).
+    int inj_row = -1, inj_k = 0, inj_bit = -1;
+    if (plan != nullptr) {
+        const InjectPlan p = plan[plan_it];
+        injected = (p.frag == f) ? 1 : 0;
+        if (injected && p.row >= r0 && p.row < r1 && ((p.row - r0) % kWarps) == warp && p.col >= c0 &&
+            p.col < c0 + 4 && p.col < N) {
+            inj_row = p.row;
+            inj_k = p.col - c0;
+            inj_bit = p.bit;
+        }
+    }
+
+    auto load = [&](int r) -> float4 {
+        const float* p = C + (long long)r * ldc + c0;
+        if (VEC) {
+            if (c0 < N) return __ldg(reinterpret_cast<const float4*>(p));
+            return make_float4(0.f, 0.f, 0.f, 0.f);
+        } else {
+            float4 v;
+            v.x = (c0 + 0 < N) ? __ldg(p + 0) : 0.f;
+            v.y = (c0 + 1 < N) ? __ldg(p + 1) : 0.f;
+            v.z = (c0 + 2 < N) ? __ldg(p + 2) : 0.f;
+            v.w = (c0 + 3 < N) ? __ldg(p + 3) : 0.f;
+            return v;
+        }
+    };
+    auto acc = [&](float4 v) {
+        acc1(v.x, s0, t0, m0);
+        acc1(v.y, s1, t1, m1);
+        acc1(v.z, s2, t2, m2);
+        acc1(v.w, s3, t3, m3);
+    };
+
+    // Batches of kBatch rows per warp, predicated, so that every load of a
+    // batch is in flight at once (one memory latency per batch).
+    for (int r = r0 + warp; r < r1; r += kBatch * kWarps) {
+        float4 v[kBatch];
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+            const int rr = r + u * kWarps;
+            v[u] = (rr < r1) ? load(rr) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        if (inj_row >= 0) {
+#pragma unroll
+            for (int u = 0; u < kBatch; ++u) {
+                if (r + u * kWarps == inj_row) {
+                    const float before = inj_k == 0 ? v[u].x : inj_k == 1 ? v[u].y : inj_k == 2 ? v[u].z : v[u].w;
+                    const float after = (inj_bit < 0) ? __fadd_rn(before, add_delta)
+                                                      : __uint_as_float(__float_as_uint(before) ^ (1u << inj_bit));
+                    if (inj_k == 0) v[u].x = after;
+                    else if (inj_k == 1) v[u].y = after;
+                    else if (inj_k == 2) v[u].z = after;
+                    else v[u].w = after;
+                    Cw[(long long)inj_row * ldc + c0 + inj_k] = after;
+                    if (log_inj) {
+                        InjectLog& L = w.ilog[plan_it];
+                        L.frag = f;
+                        L.row = inj_row;
+                        L.col = c0 + inj_k;
+                        L.bit = inj_bit;
+                        L.before = before;
+                        L.after = after;
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) acc(v[u]);
+    }
+
+    verify_tail(dsm, sel, s0, s1, s2, s3, t0, t1, t2, t3, m0, m1, m2, m3, C, ldc, M, N, total_ctas, dw_in_smem, expv,
+                tau, injected, f, F, it, w, calib_out);
+}
+
+// The same fused verify with the tile staged by the Tensor Memory Accelerator:
+// one thread keeps up to kTmaStages 32 x 128 boxes of this CTA's column strip
+// in flight (cp.async.bulk.tensor, completion on an mbarrier per stage) while
+// the eight warps accumulate from shared memory, so the HBM stream never waits
+// for the FP64 add chains. Boxes past row M or column N are zero-filled by the
+// copy engine; zeros leave S, the |x|-sum and the smallest nonzero |x| as they
+// are. rows_per is a multiple of kTmaRows, so no box crosses into the next
+// chunk. Requires a 16-byte aligned fragment and ldc % 4 == 0 (tensor map).
+__global__ void __launch_bounds__(kThreads, 2)
+    k_verify_tma(const __grid_constant__ CUtensorMap tmap, const float* __restrict__ C, long long ldc, int M, int N,
+                 int rows_per, int total_ctas, int dw_in_smem, const double* __restrict__ expv, double tau,
+                 int injected, int f, int F, int it, WsDev w, float* Cw, const InjectPlan* __restrict__ plan,
+                 int plan_it, float add_delta, int log_inj, double* calib_out) {
+    extern __shared__ __align__(1024) unsigned char ring[];
+    __shared__ SelectSmem sel;
+    __shared__ __align__(8) uint64_t full[kTmaStages];
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = blockIdx.x, chunk = blockIdx.y;
+    const int gc0 = g * kGroupCols;
+    const int c0 = gc0 + lane * 4;
+    const int r0 = chunk * rows_per;
+    const int r1 = min(M, r0 + rows_per);
+    const int nst = (r1 - r0 + kTmaRows - 1) / kTmaRows;
+
+    if (tid == 0) {
+#pragma unroll
+        for (int k = 0; k < kTmaStages; ++k) mbar_init(&full[k], 1);
+        mbar_init_fence();
+    }
+    __syncthreads();
+    if (tid == 0) {
+        const int first = min(nst, kTmaStages);
+        for (int k = 0; k < first; ++k) {
+            mbar_expect_tx(&full[k], kStageBytes);
+            tma_load_2d(ring + k * kStageBytes, &tmap, &full[k], gc0, r0 + k * kTmaRows);
+        }
+    }
+    if (chunk == 0 && tid < kGroupCols / 16 && gc0 + tid * 16 < N) prefetch_l2(expv + gc0 + tid * 16);
+
+    double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
+    float t0 = 0.f, t1 = 0.f, t2 = 0.f, t3 = 0.f;
+    uint32_t m0 = kFull, m1 = kFull, m2 = kFull, m3 = kFull;
+
+    // Graph mode: the planned fault is applied by the thread that reads the
+    // element (as in k_verify): it changes its register copy and writes C.
+    int inj_row = -1, inj_k = 0, inj_bit = -1;
+    if (plan != nullptr) {
+        const InjectPlan p = plan[plan_it];
+        injected = (p.frag == f) ? 1 : 0;
+        if (injected && p.row >= r0 && p.row < r1 && ((p.row - r0) % kWarps) == warp && p.col >= c0 &&
+            p.col < c0 + 4 && p.col < N) {
+            inj_row = p.row;
+            inj_k = p.col - c0;
+            inj_bit = p.bit;
+        }
+    }
+
+    int fault = 0, k = 0;
+    for (; k < nst; ++k) {
+        const int st = k % kTmaStages;
+        const bool got = mbar_wait(&full[st], (uint32_t)(k / kTmaStages) & 1u);
+        if (got) {
+            const float* tile = reinterpret_cast<const float*>(ring + st * kStageBytes);
+            const int rb = r0 + k * kTmaRows;
+#pragma unroll
+            for (int u = 0; u < kTmaRows / kWarps; ++u) {
+                const int rs = warp + u * kWarps;
+                const int row = rb + rs;
+                float4 v = *reinterpret_cast<const float4*>(tile + rs * kGroupCols + lane * 4);
+                if (row < r1) {
+                    if (row == inj_row) {
+                        const float before = inj_k == 0 ? v.x : inj_k == 1 ? v.y : inj_k == 2 ? v.z : v.w;
+                        const float after = (inj_bit < 0) ? __fadd_rn(before, add_delta)
+                                                          : __uint_as_float(__float_as_uint(before) ^ (1u << inj_bit));
+                        if (inj_k == 0) v.x = after;
+                        else if (inj_k == 1) v.y = after;
+                        else if (inj_k == 2) v.z = after;
+                        else v.w = after;
+                        Cw[(long long)inj_row * ldc + c0 + inj_k] = after;
+                        if (log_inj) {
+                            InjectLog& L = w.ilog[plan_it];
+                            L.frag = f;
+                            L.row = inj_row;
+                            L.col = c0 + inj_k;
+                            L.bit = inj_bit;
+                            L.before = before;
+                            L.after = after;
+                        }
+                    }
+                    acc1(v.x, s0, t0, m0);
+                    acc1(v.y, s1, t1, m1);
+                    acc1(v.z, s2, t2, m2);
+                    acc1(v.w, s3, t3, m3);
+                }
+            }
+        }
+        // every warp is done with stage st (or a wait ran out): refill it
+        if (__syncthreads_or(!got)) {
+            fault = 1;
+            break;
+        }
+        if (tid == 0 && k + kTmaStages < nst) {
+            mbar_expect_tx(&full[st], kStageBytes);
+            tma_load_2d(ring + st * kStageBytes, &tmap, &full[st], gc0, r0 + (k + kTmaStages) * kTmaRows);
+        }
+    }
+    if (fault) {
+        // A copy did not land in time: record it, give the copies still in
+        // flight a bounded chance to land, then finish the arrival protocol
+        // (the counters carry the fault; the decisions of this launch are void).
+        if (tid == 0) {
+            atomicExch(&w.ctr->fault, 1);
+            for (int j = k; j < min(nst, k + kTmaStages); ++j)
+                (void)mbar_wait(&full[j % kTmaStages], (uint32_t)(j / kTmaStages) & 1u);
+        }
+        __syncthreads();
+    }
+
+    verify_tail(ring, sel, s0, s1, s2, s3, t0, t1, t2, t3, m0, m1, m2, m3, C, ldc, M, N, total_ctas, dw_in_smem, expv,
+                tau, injected, f, F, it, w, calib_out);
 }
 
 // ----------------------------------------------------------- localise -----
@@ -755,6 +956,52 @@ void verify_geometry(int target, int M, int N, int& groups, int& chunks, int& ro
     chunks = (M + rows_per - 1) / rows_per;
 }
 
+// Geometry of the TMA-staged verify: as above, with row chunks a multiple of
+// the box height (no box crosses into the next chunk) and at least two boxes.
+void verify_geometry_tma(int target, int M, int N, int& groups, int& chunks, int& rows_per) {
+    groups = (N + kGroupCols - 1) / kGroupCols;
+    chunks = target / groups;
+    if (chunks < 1) chunks = 1;
+    if (chunks > kMaxChunks) chunks = kMaxChunks;
+    rows_per = (M + chunks - 1) / chunks;
+    rows_per = ((rows_per + kTmaRows - 1) / kTmaRows) * kTmaRows;
+    rows_per = std::max(rows_per, 2 * kTmaRows);
+    chunks = (M + rows_per - 1) / rows_per;
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// against libcuda); null when the driver does not provide it.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static std::once_flag once;
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+        (void)cudaGetLastError();
+    });
+    return fn;
+}
+
+// Tensor map of one fragment (M rows of N floats, row pitch ldc floats) with
+// kTmaRows x kGroupCols boxes, zero fill outside. False if it cannot be made.
+bool fragment_tensor_map(CUtensorMap* map, const float* Cf, int64_t ldc, int M, int N) {
+    auto enc = tensor_map_encoder();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)M};
+    const cuuint64_t strides[1] = {(cuuint64_t)ldc * sizeof(float)};
+    const cuuint32_t box[2] = {(cuuint32_t)kGroupCols, (cuuint32_t)kTmaRows};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(Cf), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Which verify body launch_verify uses: 0 = by size, 1 = 128-bit loads, 2 = TMA.
+std::atomic<int> g_verify_kernel{0};
+
 // Resident CTAs per SM of a kernel at a dynamic shared memory size (cached).
 int resident_per_sm(const void* fn, int smem) {
     static std::mutex mu;
@@ -794,6 +1041,7 @@ int ensure_kernel_attrs(int device) {
     set((const void*)k_colchain<true, false>, kColSmem);
     set((const void*)k_verify<true>, kVerifySmemMax);
     set((const void*)k_verify<false>, kVerifySmemMax);
+    set((const void*)k_verify_tma, kTmaSmem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
     done.insert(device);
     return ABFT_OK;
@@ -846,6 +1094,28 @@ int launch_verify(abft_ws* ws, const float* dC, int64_t ldc, int f, double tau, 
     const int M = ws->M_b, N = ws->counts[f];
     const float* Cf = dC + ws->offsets[f];
     if (int rc = ensure_kernel_attrs(ws->device)) return rc;
+    const double* expv = ws->d.expRow + ws->offsets[f];
+    if (it >= ws->max_iters) it = -1;
+    const InjectPlan* plan = (plan_it >= 0) ? ws->d.plan : nullptr;
+    float* Cw = const_cast<float*>(Cf);
+    int groups, chunks, rows_per;
+
+    // TMA-staged body: 16-byte aligned fragment, pitch a multiple of 4 floats,
+    // at least one full box; by default for fragments of kTmaMinBytes or more.
+    const int choice = g_verify_kernel.load(std::memory_order_relaxed);
+    const bool tma_ok = aligned16(Cf) && (ldc % 4 == 0) && N >= kGroupCols && M >= kTmaRows;
+    const bool want_tma = (choice == 2) || (choice == 0 && 4LL * M * N >= kTmaMinBytes);
+    CUtensorMap map;
+    if (tma_ok && want_tma && fragment_tensor_map(&map, Cf, ldc, M, N)) {
+        const int per_sm = resident_per_sm((const void*)k_verify_tma, kTmaSmem);
+        verify_geometry_tma(per_sm * ws->sms, M, N, groups, chunks, rows_per);
+        const int dw_in_smem = (16LL * N <= kTmaSmem) ? 1 : 0;
+        k_verify_tma<<<dim3(groups, chunks), kThreads, kTmaSmem, st>>>(
+            map, Cf, ldc, M, N, rows_per, groups * chunks, dw_in_smem, expv, tau, injected, f, ws->F, it, ws->d, Cw,
+            plan, plan_it, add_delta, log_inj, calib_out);
+        return check_launch("verify (tma)");
+    }
+
     const bool vec = aligned16(Cf) && (ldc % 4 == 0) && (N % 4 == 0);
     // d / w of the last CTA live in the 16 KB reduction area when they fit,
     // otherwise in the workspace: every CTA keeps a small shared footprint.
@@ -853,14 +1123,9 @@ int launch_verify(abft_ws* ws, const float* dC, int64_t ldc, int f, double tau, 
     const int dw_in_smem = (16LL * N <= reduce_bytes) ? 1 : 0;
     const int smem = reduce_bytes;
     const int per_sm = resident_per_sm(vec ? (const void*)k_verify<true> : (const void*)k_verify<false>, smem);
-    int groups, chunks, rows_per;
     verify_geometry(per_sm * ws->sms, M, N, groups, chunks, rows_per);
     dim3 grid(groups, chunks);
-    const double* expv = ws->d.expRow + ws->offsets[f];
-    if (it >= ws->max_iters) it = -1;
     const int total = groups * chunks;
-    const InjectPlan* plan = (plan_it >= 0) ? ws->d.plan : nullptr;
-    float* Cw = const_cast<float*>(Cf);
     if (vec)
         k_verify<true><<<grid, kThreads, smem, st>>>(Cf, ldc, M, N, rows_per, total, dw_in_smem, expv, tau,
                                                      injected, f, ws->F, it, ws->d, Cw, plan, plan_it, add_delta,
@@ -988,6 +1253,11 @@ __global__ void k_static_copyout(const FragRecord* rec, Counters* ctr, int* errc
 }
 
 }  // namespace
+
+int set_verify_kernel(int which) {
+    if (which < ABFT_VERIFY_AUTO || which > ABFT_VERIFY_TMA) return -1;
+    return g_verify_kernel.exchange(which);
+}
 
 int launch_verify_static(const float* Cf, int64_t ldc, int M, int N, const double* expv, double tau, int injected,
                          int* errcol, double* rowdiff, int* cm, cudaStream_t st) {

@@ -636,6 +636,10 @@ int abft_session_run_host(abft_session* s, const float* hA, const float* hB, flo
     r->host_ms = std::chrono::duration<double, std::milli>(h1 - h0).count();
     for (int i = 0; i < 4; ++i) r->cm[i] = hc.cm[i];
     r->n_restored = hc.n_restored;
+    if (hc.fault) {
+        set_error("verify: a bulk tensor copy did not complete within the wait limit; the decisions are void");
+        return ABFT_ERR_CUDA;
+    }
     r->kernel_launches = nl + nl2;
     r->verify_launches = nv;
     prof_stats(s, nv, r);

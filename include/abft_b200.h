@@ -164,6 +164,18 @@ int abft_calibrate(abft_ws* ws, const float* dC, int64_t ldc, int f, double* dDi
 int abft_verify_noalloc(const float* dC_frag, int64_t ldc, int M, int N, const double* dExpRow, double tau,
                         int injected, int* dErrCol, double* dRowDiff, int* dCM, void* stream);
 
+/* Which body abft_verify (and the pipeline) uses for the column sums:
+ * ABFT_VERIFY_AUTO picks by fragment size, ABFT_VERIFY_LDG streams the tile
+ * with 128-bit loads, ABFT_VERIFY_TMA stages it through shared memory with
+ * bulk tensor copies (falls back to LDG where a tensor map cannot describe
+ * the fragment: unaligned base or pitch, fewer than 128 columns or 32 rows).
+ * Decisions are identical for all three. Process-wide; returns the previous
+ * setting, or ABFT_ERR_ARG. */
+#define ABFT_VERIFY_AUTO 0
+#define ABFT_VERIFY_LDG 1
+#define ABFT_VERIFY_TMA 2
+int abft_set_verify_kernel(int which);
+
 /* Localise and correct fragment f, gated on the device by the verify result:
  * replaces launch_localize_correct (kernels/abft_stepwise.cuh:218-239).
  * dGolden (may be NULL) is the fault-free tile with leading dimension ldg,

@@ -75,3 +75,13 @@ def test_tile_injection_scheme_matches_oracle(abft, orc):
             f, r, c, b = got
             assert 0 <= r < 777 and 0 <= c < counts[f]
     assert abft.host.injection_plan_tile(5, 10, counts, offsets, "none") == (-1, -1, -1, -1)
+
+
+def test_verify_kernel_selector(abft):
+    assert abft.set_verify_kernel("ldg") == "auto"
+    assert abft.set_verify_kernel("tma") == "ldg"
+    assert abft.set_verify_kernel("auto") == "tma"
+    assert abft.lib.abft_set_verify_kernel(3) == -1
+    assert "abft_set_verify_kernel" in abft._lib.last_error()
+    with pytest.raises(KeyError):
+        abft.set_verify_kernel("fast")

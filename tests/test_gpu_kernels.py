@@ -19,7 +19,19 @@ SHAPES = [
     (1024, 1024, 1024, 4),   # 1024^3 rank tile, F = 4
     (33, 7, 9, 2),
     (2048, 64, 512, 4),
+    (1000, 96, 1032, 3),     # 16-byte aligned fragments of 344 columns: ragged last box in x and y
+    (70000, 16, 128, 1),     # tall: more row boxes per CTA than ring stages
+    (64, 8, 6400, 1),        # wide: the last CTA's d / w arrays do not fit in shared memory
 ]
+
+
+@pytest.fixture(autouse=True, params=["ldg", "tma"])
+def verify_kernel(request, abft):
+    """Every test runs with each verify body forced (TMA falls back to LDG for
+    fragments a tensor map cannot describe)."""
+    abft.set_verify_kernel(request.param)
+    yield request.param
+    abft.set_verify_kernel("auto")
 
 
 @pytest.fixture(scope="module")
@@ -132,7 +144,7 @@ def test_additive_fault_every_fragment(shape, abft, orc, torch_cuda):
             assert_same(g, o)
 
 
-@pytest.mark.parametrize("shape", [(257, 129, 515, 4), (1024, 1024, 1024, 4)])
+@pytest.mark.parametrize("shape", [(257, 129, 515, 4), (1024, 1024, 1024, 4), (1000, 96, 1032, 3)])
 def test_bitflips_all_bits(shape, abft, orc, torch_cuda):
     M, K, N, F = shape
     A, B = tiles(orc, M, K, N, 7, 8)

@@ -161,12 +161,14 @@ def test_run_host_overlapped_copies(mode, correct, repeats, abft, orc):
     s.close()
 
 
+@pytest.mark.parametrize("kernel", ["ldg", "tma"])
 @pytest.mark.parametrize("mode,zone,correct", [("swifi", "any", "inloop"), ("add", "any", "inloop"),
                                                 ("none", "any", "inloop"), ("swifi", "exponent", "drain")])
-def test_graph_mode_matches_oracle(mode, zone, correct, abft, orc):
+def test_graph_mode_matches_oracle(mode, zone, correct, kernel, abft, orc):
     """The loop replayed as a CUDA graph (injection applied inside the verify
     kernel from the device plan table) gives the same decisions, logs and
-    buffers, trial after trial with different seeds."""
+    buffers, trial after trial with different seeds; with either verify body."""
+    abft.set_verify_kernel(kernel)
     s, A, B, counts, offsets, tau, C0 = make_session(abft, orc, 1024, 512, 1024, 4, 3, 4, max_iters=12)
     golden = torch.from_numpy(C0).cuda() if mode == "swifi" else None
     s.set_golden(golden)
@@ -177,6 +179,7 @@ def test_graph_mode_matches_oracle(mode, zone, correct, abft, orc):
                             golden=C0 if mode == "swifi" else None)
         compare(s, res, o, 12)
     s.close()
+    abft.set_verify_kernel("auto")
 
 
 def test_graph_mode_uneven_and_small_fragments(abft, orc):
