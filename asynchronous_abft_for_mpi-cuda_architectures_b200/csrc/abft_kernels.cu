@@ -139,28 +139,139 @@ __device__ __forceinline__ void acc1(float x, double& s, float& t, uint32_t& m) 
     m = min(m, (__float_as_uint(x) & 0x7fffffffu) - 1u);
 }
 
+// 2^k for -1022 <= k <= 1023, built from its bits.
+__device__ __forceinline__ double pow2i(int k) { return __longlong_as_double((long long)(k + 1023) << 52); }
+
+// Exponent q of the lowest set bit of a finite nonzero double (s = odd * 2^q).
+__device__ __forceinline__ int dbl_lowbit_exp(double s) {
+    const unsigned long long b = (unsigned long long)__double_as_longlong(s);
+    const int e = (int)((b >> 52) & 0x7ff);
+    unsigned long long m = b & ((1ull << 52) - 1);
+    if (e == 0) return -1074 + (__ffsll((long long)m) - 1);
+    m |= 1ull << 52;
+    return (e - 1075) + (__ffsll((long long)m) - 1);
+}
+
+// Adds a run of terms to the sequential sum s when the result is known
+// without running the sequence: S = their sum (any order), T = their
+// |x|-sum, amax = largest |x| bits, mbm1 = smallest (|x| bits - 1) (zeros
+// excluded). Two cases are decided exactly:
+//  * no rounding: s and every term are multiples of 2^p and |s| + T <= 2^(p+53),
+//    so every sequential partial sum is representable, and so are S and s + S;
+//  * absorption: every |x| < ulp(s) / 4, so each sequential add rounds back to s.
+// Returns false (s unchanged) when neither applies or a term is Inf / NaN.
+__device__ __forceinline__ bool run_shortcut(double& s, double S, double T, uint32_t amax, uint32_t mbm1) {
+    if (amax >= 0x7f800000u || !isfinite(s)) return false;
+    constexpr int kNone = 1 << 30;
+    int p = (mbm1 == kFull) ? kNone : max((int)((mbm1 + 1u) >> 23), 1) - 150;
+    if (s != 0.0) p = min(p, dbl_lowbit_exp(s));
+    if (p == kNone) return true;  // s == +0 and every term is +-0: s stays +0
+    if (p + 53 <= 1023 && (fabs(s) + T) * (1.0 + 0x1p-40) <= pow2i(p + 53)) {
+        s = s + S;
+        return true;
+    }
+    if (s != 0.0) {
+        const int es = (int)(((unsigned long long)__double_as_longlong(s) >> 52) & 0x7ff);
+        if (es >= 55 && (double)__uint_as_float(amax) < pow2i(es - 1077)) return true;
+    }
+    return false;
+}
+
+// s += lane 0's value, then lane 1's, ... lane m-1's, one rounding each
+// (m is warp-uniform).
+__device__ __forceinline__ void seq_run(double& s, float v, int m) {
+    if (m >= 32) {
+#pragma unroll
+        for (int r = 0; r < 32; ++r) s = __dadd_rn(s, (double)__shfl_sync(kFull, v, r));
+    } else {
+        for (int r = 0; r < m; ++r) s = __dadd_rn(s, (double)__shfl_sync(kFull, v, r));
+    }
+}
+
+// Warp-wide statistics of one value per lane, folded into a block's.
+__device__ __forceinline__ void warp_stats(double& S, double& T, uint32_t& amax, uint32_t& mbm1) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        S += __shfl_xor_sync(kFull, S, o);
+        T += __shfl_xor_sync(kFull, T, o);
+    }
+    amax = __reduce_max_sync(kFull, amax);
+    mbm1 = __reduce_min_sync(kFull, mbm1);
+}
+
 // Sequential double sum x[0] + x[stride] + ... (n terms) in ascending order,
-// starting from 0.0: the reference's per-thread loop. Warp-cooperative: lanes
-// prefetch 32 terms (through L2: the verify kernel may have written one of
-// them in graph mode), every lane runs the same chain.
-__device__ double exact_chain(const float* __restrict__ x, long long stride, int n) {
+// starting from 0.0: the reference's per-thread loop, bit for bit.
+// Warp-cooperative: lane l holds terms l, l + 32, ... of a 128-term block
+// (loaded through L2, one block ahead: the verify kernel may have written one
+// of them in graph mode). A block, else each of its 32-term runs, is added in
+// one step when run_shortcut proves the sequential result; only the remaining
+// runs execute their 32 dependent adds (all runs, once two consecutive blocks
+// offered no shortcut, so that hard columns cost no more than the plain chain).
+__device__ __forceinline__ double exact_chain(const float* __restrict__ x, long long stride, int n) {
+    constexpr int U = 4;
     const int lane = threadIdx.x & 31;
     double s = 0.0;
-    float v = (lane < n) ? __ldcg(x + (long long)lane * stride) : 0.f;
-    for (int i0 = 0; i0 < n; i0 += 32) {
-        const int nx = i0 + 32 + lane;
-        const float vn = (nx < n) ? __ldcg(x + (long long)nx * stride) : 0.f;
-        if (n - i0 >= 32) {
+    int hard = 0;  // consecutive blocks in which no run could be shortcut
+    int b0 = 0;
+    {
+        float v[U], vn[U];
 #pragma unroll
-            for (int r = 0; r < 32; ++r) s = __dadd_rn(s, (double)__shfl_sync(kFull, v, r));
-        } else {
-            const int m = n - i0;
-            for (int r = 0; r < 32; ++r) {
-                const float y = __shfl_sync(kFull, v, r);
-                if (r < m) s = __dadd_rn(s, (double)y);
-            }
+        for (int u = 0; u < U; ++u) {
+            const int i = u * 32 + lane;
+            v[u] = (i < n) ? __ldcg(x + (long long)i * stride) : 0.f;
         }
-        v = vn;
+        for (; b0 < n && hard < 2; b0 += 32 * U) {
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int i = b0 + 32 * U + u * 32 + lane;
+                vn[u] = (i < n) ? __ldcg(x + (long long)i * stride) : 0.f;
+            }
+            double S = 0.0, T = 0.0;
+            uint32_t amax = 0u, mbm1 = kFull;
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const uint32_t a = __float_as_uint(v[u]) & 0x7fffffffu;
+                S += (double)v[u];
+                T += (double)__uint_as_float(a);
+                amax = max(amax, a);
+                mbm1 = min(mbm1, a - 1u);
+            }
+            warp_stats(S, T, amax, mbm1);
+            if (run_shortcut(s, S, T, amax, mbm1)) {
+                hard = 0;
+            } else {
+                bool any = false;
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const int c0 = b0 + u * 32;
+                    if (c0 >= n) break;
+                    const uint32_t a = __float_as_uint(v[u]) & 0x7fffffffu;
+                    double Sc = (double)v[u], Tc = (double)__uint_as_float(a);
+                    uint32_t ac = a, mc = a - 1u;
+                    warp_stats(Sc, Tc, ac, mc);
+                    if (run_shortcut(s, Sc, Tc, ac, mc)) {
+                        any = true;
+                        continue;
+                    }
+                    seq_run(s, v[u], min(32, n - c0));
+                }
+                hard = any ? 0 : hard + 1;
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) v[u] = vn[u];
+        }
+    }
+    // Two blocks in a row offered no shortcut: the column is hard and the
+    // statistics would only add cost. The rest runs as the plain chain, 32
+    // terms prefetched ahead.
+    if (b0 < n) {
+        float v = (b0 + lane < n) ? __ldcg(x + (long long)(b0 + lane) * stride) : 0.f;
+        for (int i0 = b0; i0 < n; i0 += 32) {
+            const int nx = i0 + 32 + lane;
+            const float vn = (nx < n) ? __ldcg(x + (long long)nx * stride) : 0.f;
+            seq_run(s, v, min(32, n - i0));
+            v = vn;
+        }
     }
     return s;
 }

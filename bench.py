@@ -49,6 +49,8 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-graph", action="store_true", help="enqueue the loop from the host every trial")
     p.add_argument("--no-cpu", action="store_true")
+    p.add_argument("--verify-kernel", choices=["auto", "ldg", "tma"], default="auto",
+                   help="verify body: by fragment size, 128-bit loads, or TMA-staged")
     return p.parse_args()
 
 
@@ -63,6 +65,7 @@ def workload(args, Pr, Pc):
         "l2": "inputs larger than L2 (A, B, 2 x C per rank = 256 MiB > 126 MB)",
         "parallelism": f"{Pr}x{Pc} output-tile grid, one rank per GPU",
         "loop": "host-enqueued" if args.no_graph else "CUDA graph per trial",
+        "verify_kernel": args.verify_kernel,
     }
 
 
@@ -259,6 +262,7 @@ def run_ours(args):
     import torch
 
     abft = importlib.import_module(PKG)
+    abft.set_verify_kernel(args.verify_kernel)
     from importlib import import_module
     dist_mod = import_module(f"{PKG}.distributed")
     rank, world, local = dist_mod.init_from_env(timeout_s=300)

@@ -304,3 +304,86 @@ def test_calibrate_exact_diffs(shape, abft, orc, torch_cuda):
         w = want[offsets[f]:offsets[f] + counts[f]]
         assert np.array_equal(got[f].view(np.uint64), w.view(np.uint64))
     ws.close()
+
+
+def adversarial(rng, n, kind):
+    """One line of n float32 terms built to defeat the any-order certificate."""
+    x = (rng.standard_normal(n) * 30).astype(np.float32)
+    r = int(rng.integers(0, n))
+    if kind == 1:
+        x[r] *= np.float32(2.0 ** -40)                      # one tiny term
+    elif kind == 2:
+        x[r] *= np.float32(2.0 ** 40)                       # one huge term
+    elif kind == 3:
+        r2 = int(rng.integers(r, n))
+        x[r], x[r2] = 3.0e30, -3.0e30                        # huge, later cancelled
+    elif kind == 4:
+        idx = rng.integers(0, n, 7)
+        x[idx] = (rng.integers(1, 1 << 20, 7) * np.float32(2.0 ** -149)).astype(np.float32)  # subnormals
+    elif kind == 5:
+        x *= np.exp2(rng.integers(-60, 61, n)).astype(np.float32)   # magnitudes over 2^+-60
+    elif kind == 6:
+        x[0] = 1.0e30                                         # absorbs everything after it
+    elif kind == 7:
+        k = np.arange(n)
+        x = ((1.0 + (k % 97) * 2.0 ** -23) * np.where(k % 2, -1.0, 1.0)).astype(np.float32)
+    elif kind == 8:
+        x[:] = -0.0
+        x[r] = 1.5
+    elif kind == 9:
+        x[:] = 2.0 ** -27
+        x[0] = 2.0 ** 30
+    elif kind == 10:
+        x[n // 2] = 1.0e35
+        x[-1] = -1.0e35
+    elif kind == 11:
+        x *= np.float32(2.0 ** -100)
+        x[r] = 7.0
+    elif kind == 12:
+        h = n // 3                                            # a hard stretch, then plain terms
+        x[:h] *= np.exp2(rng.integers(-60, 61, h)).astype(np.float32)
+    return x
+
+
+@pytest.mark.parametrize("M", [3000, 257])
+def test_exact_chain_adversarial_columns(M, abft, orc, torch_cuda):
+    """Calibration re-sums every uncertified column in the reference's order:
+    each must equal the sequential double sum bit for bit, whatever mix of
+    tiny, huge, subnormal, cancelling and absorbed terms the column holds."""
+    torch = torch_cuda
+    rng = np.random.default_rng(2024 + M)
+    K, N, F = 16, 512, 2
+    A, B = tiles(orc, M, K, N, 71, 72)
+    counts, offsets = orc.split_dim(N, F)
+    C = np.empty((M, N), np.float32)
+    for j in range(N):
+        C[:, j] = adversarial(rng, M, j % 13)
+    ws = abft.kernels.Workspace(M, N, K, counts, offsets)
+    dA, dB, dC = to_dev(torch, A), to_dev(torch, B), to_dev(torch, C)
+    abft.kernels.encode(ws, dA, dB)
+    got = [abft.kernels.calibrate(ws, dC, f).cpu().numpy() for f in range(F)]
+    torch.cuda.synchronize()
+    _, expRow, _, _ = orc.encode(A, B, counts, offsets)
+    want = np.abs(orc.actual_row(C) - expRow)
+    for f in range(F):
+        w = want[offsets[f]:offsets[f] + counts[f]]
+        assert np.array_equal(got[f].view(np.uint64), w.view(np.uint64))
+    ws.close()
+
+
+def test_exact_chain_adversarial_rows(abft, orc, torch_cuda):
+    """The same patterns along rows, with a fault to localise: the row arg-max
+    re-sums its uncertified candidate rows exactly."""
+    rng = np.random.default_rng(77)
+    M, K, N, F = 600, 16, 1200, 2
+    A, B = tiles(orc, M, K, N, 73, 74)
+    counts, offsets = orc.split_dim(N, F)
+    C0 = np.empty((M, N), np.float32)
+    for i in range(M):
+        C0[i, :] = adversarial(rng, N, i % 13)
+    for f, (r, c) in enumerate([(37, 5), (300, 200)]):
+        C = add_fault(C0, r, offsets[f] + c, 1.0e6)
+        for tau in (1.0e3, 1.0e5):
+            g = run_gpu_iteration(abft, torch_cuda, A, B, C, counts, offsets, [tau] * F, f, golden=C0)
+            o = run_oracle_iteration(orc, A, B, C, counts, offsets, [tau] * F, f, golden=C0)
+            assert_same(g, o)
