@@ -77,9 +77,12 @@ def peak_hbm():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def verify_traffic_per_launch(tile, frags):
-    """DRAM bytes per verify launch from the committed ncu summary of this fragment shape, if any."""
-    path = os.path.join(ROOT, "profiles", f"verify_{tile}x{tile // frags}.md")
+def verify_traffic_per_launch(tile, frags, kernel):
+    """DRAM bytes per verify launch from the committed ncu summary of this fragment
+    shape and verify body, if any (fragments below 512 MiB run the 128-bit-load
+    body unless the TMA one is forced)."""
+    body = "verify_tma" if kernel == "tma" else "verify"
+    path = os.path.join(ROOT, "profiles", f"{body}_{tile}x{tile // frags}.md")
     try:
         with open(path) as f:
             for line in f:
@@ -369,7 +372,7 @@ def run_ours(args):
         live_gbs = bytes_launch / (v_avg_max[0] * 1e-3) / 1e9 if v_avg_max[0] > 0 else None
         iso_gbs = bytes_launch / (v_avg_max[1] * 1e-3) / 1e9 if v_avg_max[1] > 0 else None
         large_gbs = large_bytes / (large_ms * 1e-3) / 1e9 if large_ms > 0 else None
-        traffic = verify_traffic_per_launch(args.tile, args.frags)
+        traffic = verify_traffic_per_launch(args.tile, args.frags, args.verify_kernel)
         line = {
             "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": total_p / args.steps, "higher_is_better": True,
