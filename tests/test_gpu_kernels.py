@@ -22,6 +22,10 @@ SHAPES = [
     (1000, 96, 1032, 3),     # 16-byte aligned fragments of 344 columns: ragged last box in x and y
     (70000, 16, 128, 1),     # tall: more row boxes per CTA than ring stages
     (64, 8, 6400, 1),        # wide: the last CTA's d / w arrays do not fit in shared memory
+    (1, 1, 1, 1),            # degenerate tiles
+    (1, 3, 5, 1),
+    (5, 1, 7, 2),
+    (2, 2, 4, 4),            # one column per fragment
 ]
 
 
@@ -112,6 +116,43 @@ def test_encode_strided_and_unaligned(abft, orc, torch_cuda):
     want = orc.encode(A, B, counts, offsets)
     for g, w in zip(got, want):
         assert np.array_equal(g.view(np.uint64), w.view(np.uint64))
+
+
+@pytest.mark.parametrize("pad,shift", [(12, 4), (5, 1)])
+def test_verify_localize_on_views(pad, shift, abft, orc, torch_cuda):
+    """C as a view into a wider buffer (leading dimension > width): 16-byte
+    aligned with ldc % 4 == 0 (the TMA body takes it), or shifted by one float
+    (128-bit loads impossible). Decisions and corrections equal the oracle's
+    and the padding around the view is never written."""
+    torch = torch_cuda
+    M, K, N, F = 700, 64, 1032, 3
+    A, B = tiles(orc, M, K, N, 81, 82)
+    counts, offsets = orc.split_dim(N, F)
+    C0 = product_f64(A, B)
+    tau = [1e-2] * F
+    kern = abft.kernels
+    dA, dB, dG = to_dev(torch, A), to_dev(torch, B), to_dev(torch, C0)
+    for f in range(F):
+        C = add_fault(C0, 123 + f, offsets[f] + 7 * f + 1, 1.0e6)
+        Cw = np.full((M, N + pad), np.nan, np.float32)
+        Cw[:, shift:shift + N] = C
+        dCw = to_dev(torch, Cw)
+        dC = dCw[:, shift:shift + N]
+        ws = kern.Workspace(M, N, K, counts, offsets, max_iters=1)
+        kern.encode(ws, dA, dB)
+        ws.reset_counters()
+        for g in range(F):
+            kern.verify(ws, dC, g, tau[g], injected=(g == f), it=0)
+            kern.localize_correct(ws, dC, g, tau[g], injected=(g == f), golden=dG, it=0)
+        torch.cuda.synchronize()
+        cm, nr = ws.counters()
+        ec, er, rd = ws.read_log(1)
+        out = dCw.cpu().numpy()
+        ws.close()
+        o = run_oracle_iteration(orc, A, B, C, counts, offsets, tau, f, golden=C0)
+        assert_same(dict(cm=cm, nr=nr, ec=ec[0], er=er[0], rd=rd[0], C=np.ascontiguousarray(out[:, shift:shift + N])),
+                    o)
+        assert np.isnan(out[:, :shift]).all() and np.isnan(out[:, shift + N:]).all()
 
 
 @pytest.mark.parametrize("shape", SHAPES)
