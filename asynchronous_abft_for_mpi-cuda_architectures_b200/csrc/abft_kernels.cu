@@ -1051,7 +1051,6 @@ int check_launch(const char* what) {
     return ABFT_OK;
 }
 
-// Verify geometry: column groups x row chunks, about two CTAs per SM.
 // Verify geometry: column groups x row chunks, sized to one full wave of
 // resident CTAs (target = resident CTAs per SM x SMs; a second, mostly empty
 // wave would double the launch time).

@@ -580,71 +580,82 @@ int abft_session_run_host(abft_session* s, const float* hA, const float* hB, flo
     RC(ensure_prof_events(s, a->repeats * s->F));
     CK(cudaStreamSynchronize(s->verify));
     CK(cudaStreamSynchronize(s->compute));
-    const auto h0 = std::chrono::high_resolution_clock::now();
-    CK(cudaEventRecord(s->t0, s->compute));
-    CK(cudaStreamWaitEvent(s->xfer, s->t0, 0));
-    // inputs: host -> device on the copy stream, A first, then B one fragment
-    // (column block) at a time; iteration 0's SGEMM of fragment f starts as
-    // soon as A and B's fragment f are in.
-    CK(cudaMemcpy2DAsync(const_cast<float*>(s->dA), sizeof(float) * s->lda, hA, sizeof(float) * s->K,
-                         sizeof(float) * s->K, s->M_b, cudaMemcpyHostToDevice, s->xfer));
-    CK(cudaEventRecord(s->a_in, s->xfer));
-    for (int f = 0; f < s->F; ++f) {
-        const int off = s->offsets[f];
-        CK(cudaMemcpy2DAsync(const_cast<float*>(s->dB) + off, sizeof(float) * s->ldb, hB + off,
-                             sizeof(float) * s->N_b, sizeof(float) * s->counts[f], s->K, cudaMemcpyHostToDevice,
-                             s->xfer));
-        CK(cudaEventRecord(s->b_in[f], s->xfer));
+    // Enqueue and wait; on an error part of the work may still be queued, and
+    // copies into the caller's host buffers must not outlive this call.
+    auto run = [&]() -> int {
+        const auto h0 = std::chrono::high_resolution_clock::now();
+        CK(cudaEventRecord(s->t0, s->compute));
+        CK(cudaStreamWaitEvent(s->xfer, s->t0, 0));
+        // inputs: host -> device on the copy stream, A first, then B one fragment
+        // (column block) at a time; iteration 0's SGEMM of fragment f starts as
+        // soon as A and B's fragment f are in.
+        CK(cudaMemcpy2DAsync(const_cast<float*>(s->dA), sizeof(float) * s->lda, hA, sizeof(float) * s->K,
+                             sizeof(float) * s->K, s->M_b, cudaMemcpyHostToDevice, s->xfer));
+        CK(cudaEventRecord(s->a_in, s->xfer));
+        for (int f = 0; f < s->F; ++f) {
+            const int off = s->offsets[f];
+            CK(cudaMemcpy2DAsync(const_cast<float*>(s->dB) + off, sizeof(float) * s->ldb, hB + off,
+                                 sizeof(float) * s->N_b, sizeof(float) * s->counts[f], s->K, cudaMemcpyHostToDevice,
+                                 s->xfer));
+            CK(cudaEventRecord(s->b_in[f], s->xfer));
+        }
+        // the checksums need all of B: encoded on the verify stream while the
+        // first SGEMMs run
+        CK(cudaStreamWaitEvent(s->verify, s->b_in[s->F - 1], 0));
+        int nl = 0, nv = 0;
+        RC(abft_ws_reset_counters(s->ws, s->verify));
+        RC(launch_encode(s->ws, s->dA, s->lda, s->dB, s->ldb, s->verify, &nl));
+        s->encoded = true;
+        // result: device -> host. With in-loop correction each fragment of the
+        // final buffer is final once its last verification and correction ran,
+        // and is copied then; drain correction rewrites the buffer after the loop.
+        const bool drain = (a->mode == ABFT_INJECT_ADD || a->mode == ABFT_INJECT_SWIFI) &&
+                           a->correct_mode == ABFT_CORRECT_DRAIN;
+        const IoHooks io{s->a_in, s->b_in.data(), drain ? nullptr : s->c_out.data()};
+        int nl2 = 0;
+        RC(enqueue_loop(s, a, plan, &nl2, &nv, false, &io));
+        CK(cudaEventRecord(s->vjoin, s->verify));
+        const float* last = s->dC[(a->repeats - 1) & 1];
+        if (drain) CK(cudaStreamWaitEvent(s->xfer, s->vjoin, 0));
+        for (int f = 0; f < s->F; ++f) {
+            const int off = s->offsets[f];
+            if (!drain) CK(cudaStreamWaitEvent(s->xfer, s->c_out[f], 0));
+            CK(cudaMemcpy2DAsync(hC + off, sizeof(float) * s->N_b, last + off, sizeof(float) * s->ldc,
+                                 sizeof(float) * s->counts[f], s->M_b, cudaMemcpyDeviceToHost, s->xfer));
+        }
+        CK(cudaEventRecord(s->xjoin, s->xfer));
+        CK(cudaStreamWaitEvent(s->compute, s->vjoin, 0));
+        CK(cudaStreamWaitEvent(s->compute, s->xjoin, 0));
+        Counters hc{};
+        CK(cudaMemcpyAsync(&hc, s->ws->d.ctr, sizeof(hc), cudaMemcpyDeviceToHost, s->compute));
+        CK(cudaEventRecord(s->t1, s->compute));
+        CK(cudaEventSynchronize(s->t1));
+        const auto h1 = std::chrono::high_resolution_clock::now();
+        CK(cudaGetLastError());
+        float ms = 0.f;
+        CK(cudaEventElapsedTime(&ms, s->t0, s->t1));
+        if (e2e_ms) *e2e_ms = ms;
+        r->device_ms = ms;
+        r->host_ms = std::chrono::duration<double, std::milli>(h1 - h0).count();
+        for (int i = 0; i < 4; ++i) r->cm[i] = hc.cm[i];
+        r->n_restored = hc.n_restored;
+        if (hc.fault) {
+            set_error("verify: a bulk tensor copy did not complete within the wait limit; the decisions are void");
+            return ABFT_ERR_CUDA;
+        }
+        r->kernel_launches = nl + nl2;
+        r->verify_launches = nv;
+        prof_stats(s, nv, r);
+        s->last_launches = nl + nl2;
+        return ABFT_OK;
+    };
+    const int rc = run();
+    if (rc != ABFT_OK) {
+        cudaStreamSynchronize(s->xfer);
+        cudaStreamSynchronize(s->verify);
+        cudaStreamSynchronize(s->compute);
     }
-    // the checksums need all of B: encoded on the verify stream while the
-    // first SGEMMs run
-    CK(cudaStreamWaitEvent(s->verify, s->b_in[s->F - 1], 0));
-    int nl = 0, nv = 0;
-    RC(abft_ws_reset_counters(s->ws, s->verify));
-    RC(launch_encode(s->ws, s->dA, s->lda, s->dB, s->ldb, s->verify, &nl));
-    s->encoded = true;
-    // result: device -> host. With in-loop correction each fragment of the
-    // final buffer is final once its last verification and correction ran,
-    // and is copied then; drain correction rewrites the buffer after the loop.
-    const bool drain = (a->mode == ABFT_INJECT_ADD || a->mode == ABFT_INJECT_SWIFI) &&
-                       a->correct_mode == ABFT_CORRECT_DRAIN;
-    const IoHooks io{s->a_in, s->b_in.data(), drain ? nullptr : s->c_out.data()};
-    int nl2 = 0;
-    RC(enqueue_loop(s, a, plan, &nl2, &nv, false, &io));
-    CK(cudaEventRecord(s->vjoin, s->verify));
-    const float* last = s->dC[(a->repeats - 1) & 1];
-    if (drain) CK(cudaStreamWaitEvent(s->xfer, s->vjoin, 0));
-    for (int f = 0; f < s->F; ++f) {
-        const int off = s->offsets[f];
-        if (!drain) CK(cudaStreamWaitEvent(s->xfer, s->c_out[f], 0));
-        CK(cudaMemcpy2DAsync(hC + off, sizeof(float) * s->N_b, last + off, sizeof(float) * s->ldc,
-                             sizeof(float) * s->counts[f], s->M_b, cudaMemcpyDeviceToHost, s->xfer));
-    }
-    CK(cudaEventRecord(s->xjoin, s->xfer));
-    CK(cudaStreamWaitEvent(s->compute, s->vjoin, 0));
-    CK(cudaStreamWaitEvent(s->compute, s->xjoin, 0));
-    Counters hc{};
-    CK(cudaMemcpyAsync(&hc, s->ws->d.ctr, sizeof(hc), cudaMemcpyDeviceToHost, s->compute));
-    CK(cudaEventRecord(s->t1, s->compute));
-    CK(cudaEventSynchronize(s->t1));
-    const auto h1 = std::chrono::high_resolution_clock::now();
-    CK(cudaGetLastError());
-    float ms = 0.f;
-    CK(cudaEventElapsedTime(&ms, s->t0, s->t1));
-    if (e2e_ms) *e2e_ms = ms;
-    r->device_ms = ms;
-    r->host_ms = std::chrono::duration<double, std::milli>(h1 - h0).count();
-    for (int i = 0; i < 4; ++i) r->cm[i] = hc.cm[i];
-    r->n_restored = hc.n_restored;
-    if (hc.fault) {
-        set_error("verify: a bulk tensor copy did not complete within the wait limit; the decisions are void");
-        return ABFT_ERR_CUDA;
-    }
-    r->kernel_launches = nl + nl2;
-    r->verify_launches = nv;
-    prof_stats(s, nv, r);
-    s->last_launches = nl + nl2;
-    return ABFT_OK;
+    return rc;
 }
 
 }  // extern "C"
