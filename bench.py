@@ -51,6 +51,10 @@ def parse():
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--verify-kernel", choices=["auto", "ldg", "tma"], default="auto",
                    help="verify body: by fragment size, 128-bit loads, or TMA-staged")
+    p.add_argument("--timeline", default=None, metavar="TRACE_JSON",
+                   help="after the timed runs, record one protected trial with the CUDA profiler (CUPTI "
+                        "kernel records, cuBLAS included) into this Chrome trace and report how much of "
+                        "the ABFT kernels' time overlapped an SGEMM")
     return p.parse_args()
 
 
@@ -260,6 +264,53 @@ def isolated_verify_large(abft, torch, device, M=16384, N=4096, reps=5):
     return 4.0 * M * N + 24.0 * N, statistics.median(times)
 
 
+def overlap_timeline(torch, s, args, base, rank, path):
+    """One protected trial under torch.profiler: every kernel's device start and
+    end (CUPTI), written as a Chrome trace. Reports, per ABFT kernel, the share
+    of its device time during which an SGEMM kernel was also running."""
+    import re
+    from torch.profiler import ProfilerActivity, profile
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        s.online(args.mode, args.zone, base_seed=base, rank=rank, repeats=args.iters, graph=not args.no_graph)
+        torch.cuda.synchronize()
+    prof.export_chrome_trace(path)
+    with open(path) as f:
+        events = json.load(f).get("traceEvents", [])
+    kern = [e for e in events if e.get("cat") == "kernel" and "dur" in e]
+    gemm = sorted((float(e["ts"]), float(e["ts"]) + float(e["dur"])) for e in kern if "sgemm" in e["name"].lower())
+    busy = []
+    for a, b in gemm:
+        if busy and a <= busy[-1][1]:
+            busy[-1][1] = max(busy[-1][1], b)
+        else:
+            busy.append([a, b])
+
+    def under_gemm(a, b):
+        return sum(max(0.0, min(b, y) - max(a, x)) for x, y in busy)
+
+    per = {}
+    for e in kern:
+        m = re.search(r"abft::.*?(k_\w+)", e["name"])
+        if not m:
+            continue
+        a, b = float(e["ts"]), float(e["ts"]) + float(e["dur"])
+        d = per.setdefault(m.group(1), [0, 0.0, 0.0])
+        d[0] += 1
+        d[1] += b - a
+        d[2] += under_gemm(a, b)
+    tot = sum(v[1] for v in per.values())
+    return {
+        "trace": path, "iters": args.iters, "sgemm_launches": len(gemm),
+        "sgemm_us": sum(b - a for a, b in gemm),
+        "span_us": (max(float(e["ts"]) + float(e["dur"]) for e in kern) - min(float(e["ts"]) for e in kern))
+        if kern else 0.0,
+        "abft_us": tot,
+        "abft_overlapped_pct": 100.0 * sum(v[2] for v in per.values()) / tot if tot else None,
+        "kernels": {k: {"launches": v[0], "us": v[1], "overlapped_pct": 100.0 * v[2] / v[1] if v[1] else None}
+                    for k, v in sorted(per.items())},
+    }
+
+
 def run_ours(args):
     import numpy as np
     import torch
@@ -359,6 +410,7 @@ def run_ours(args):
                "sample": f"{r['iters']} protected iteration(s) of the {t.M_b}x{t.N_b}x{K} tile "
                          f"(numpy SGEMM + oracle verification/localisation/correction), {r['seconds']:.1f} s"}
 
+    tl = overlap_timeline(torch, s, args, base, rank, args.timeline) if (args.timeline and rank == 0) else None
     s.close()
     if rank == 0:
         flops_step = 2.0 * M * N * K * args.iters
@@ -413,6 +465,8 @@ def run_ours(args):
                            "path": "OnlineSession.run_host -> abft_session_run_host (pinned host in/out)"}
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        if tl is not None:
+            line["timeline"] = tl
         print(json.dumps(line), flush=True)
     dist_mod.shutdown()
 
