@@ -112,10 +112,11 @@ WsLayout ws_layout(int M_b, int N_b, int K, int F, int nfmax, int max_iters);
 int launch_encode(abft_ws* ws, const float* dA, int64_t lda, const float* dB, int64_t ldb, cudaStream_t st,
                   int* launches);
 // plan_it >= 0 selects graph mode: the injection of iteration plan_it is read
-// from ws->d.plan on the device (verify applies it, log_inj logs it).
+// from ws->d.plan on the device (verify applies it, log_inj logs it). cond:
+// a graph conditional handle the kernel sets to "column detected" (0: none).
 int launch_verify(abft_ws* ws, const float* dC, int64_t ldc, int f, double tau, int injected, int it,
                   cudaStream_t st, int plan_it = -1, float add_delta = 0.f, int log_inj = 0,
-                  double* calib_out = nullptr);
+                  double* calib_out = nullptr, unsigned long long cond = 0);
 int launch_localize(abft_ws* ws, float* dC, int64_t ldc, int f, double tau, int injected, const float* dG,
                     int64_t ldg, int it, int correct_mode, cudaStream_t st, int plan_it = -1);
 int launch_drain(abft_ws* ws, float* dC0, float* dC1, int64_t ldc, const float* dG, int64_t ldg, int repeats,

@@ -47,6 +47,7 @@ namespace {
 constexpr unsigned kFull = 0xffffffffu;
 constexpr int kListCap = 256;
 constexpr int kBatch = 8;   // rows in flight per warp in the verify body
+constexpr int kLocNarrow = 512;  // localise: rows of at most this many floats are summed 4 per warp at a time
 // TMA-staged verify: 32-row x 128-column boxes (16 KB) through a 6-stage ring.
 constexpr int kTmaRows = 32;
 constexpr int kTmaStages = 6;
@@ -414,7 +415,8 @@ __device__ __forceinline__ void verify_tail(unsigned char* dsm, SelectSmem& sel,
                                             uint32_t m1, uint32_t m2, uint32_t m3, const float* __restrict__ C,
                                             long long ldc, int M, int N, int total_ctas, int dw_in_smem,
                                             const double* __restrict__ expv, double tau, int injected, int f, int F,
-                                            int it, const WsDev& w, double* calib_out) {
+                                            int it, const WsDev& w, double* calib_out,
+                                            cudaGraphConditionalHandle cond) {
     double(*s_s)[kGroupCols] = reinterpret_cast<double(*)[kGroupCols]>(dsm);
     float(*s_t)[kGroupCols] = reinterpret_cast<float(*)[kGroupCols]>(dsm + kWarps * kGroupCols * 8);
     uint32_t(*s_m)[kGroupCols] = reinterpret_cast<uint32_t(*)[kGroupCols]>(dsm + kWarps * kGroupCols * 12);
@@ -510,6 +512,9 @@ __device__ __forceinline__ void verify_tail(unsigned char* dsm, SelectSmem& sel,
         const int det = ec >= 0;
         const int idx = injected ? (det ? 0 : 3) : (det ? 2 : 1);
         atomicAdd(&w.ctr->cm[idx], 1);
+        // graph mode: the localisation node of this fragment runs only if a
+        // column was detected
+        if (cond != 0) cudaGraphSetConditional(cond, det ? 1u : 0u);
         if (it >= 0) {
             DecisionLog& L = w.dlog[(long long)it * F + f];
             L.errcol = ec;
@@ -534,7 +539,7 @@ __global__ void __launch_bounds__(kThreads, 4)
     k_verify(const float* __restrict__ C, long long ldc, int M, int N, int rows_per, int total_ctas, int dw_in_smem,
              const double* __restrict__ expv, double tau, int injected, int f, int F, int it, WsDev w,
              float* Cw, const InjectPlan* __restrict__ plan, int plan_it, float add_delta, int log_inj,
-             double* calib_out) {
+             double* calib_out, cudaGraphConditionalHandle cond) {
     extern __shared__ __align__(16) unsigned char dsm[];
     __shared__ SelectSmem sel;
 
@@ -627,7 +632,7 @@ __global__ void __launch_bounds__(kThreads, 4)
     }
 
     verify_tail(dsm, sel, s0, s1, s2, s3, t0, t1, t2, t3, m0, m1, m2, m3, C, ldc, M, N, total_ctas, dw_in_smem, expv,
-                tau, injected, f, F, it, w, calib_out);
+                tau, injected, f, F, it, w, calib_out, cond);
 }
 
 // The same fused verify with the tile staged by the Tensor Memory Accelerator:
@@ -642,7 +647,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     k_verify_tma(const __grid_constant__ CUtensorMap tmap, const float* __restrict__ C, long long ldc, int M, int N,
                  int rows_per, int total_ctas, int dw_in_smem, const double* __restrict__ expv, double tau,
                  int injected, int f, int F, int it, WsDev w, float* Cw, const InjectPlan* __restrict__ plan,
-                 int plan_it, float add_delta, int log_inj, double* calib_out) {
+                 int plan_it, float add_delta, int log_inj, double* calib_out, cudaGraphConditionalHandle cond) {
     extern __shared__ __align__(1024) unsigned char ring[];
     __shared__ SelectSmem sel;
     __shared__ __align__(8) uint64_t full[kTmaStages];
@@ -750,15 +755,15 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
 
     verify_tail(ring, sel, s0, s1, s2, s3, t0, t1, t2, t3, m0, m1, m2, m3, C, ldc, M, N, total_ctas, dw_in_smem, expv,
-                tau, injected, f, F, it, w, calib_out);
+                tau, injected, f, F, it, w, calib_out, cond);
 }
 
 // ----------------------------------------------------------- localise -----
 
 // Gated localisation + correction for one fragment: row sums of the fragment
-// (warp per row), certified like the column sums, then the reference's row
+// (a warp sums ROWS rows side by side), certified like the column sums, then the reference's row
 // arg-max (k_locate_correct) and the correction C = float(double(C) - rowdiff).
-template <bool VEC>
+template <bool VEC, int ROWS>
 __global__ void __launch_bounds__(kThreads)
     k_localize(float* C, long long ldc, int M, int N, int rows_per, int nblocks, const double* __restrict__ expc,
                double tau, int injected, const float* __restrict__ G, long long ldg, int frag_off, int f, int F,
@@ -770,35 +775,78 @@ __global__ void __launch_bounds__(kThreads)
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int r0 = blockIdx.x * rows_per;
     const int r1 = min(M, r0 + rows_per);
-    for (int r = r0 + warp; r < r1; r += kWarps) {
-        const float* row = C + (long long)r * ldc;
-        double s = 0.0;
-        float t = 0.f;
-        uint32_t m = kFull;
+    // ROWS rows per warp at a time, independent accumulators: their loads and
+    // add chains overlap instead of paying one latency per row (narrow rows);
+    // a single row keeps 4 loads per lane in flight along the row instead.
+    for (int rb = r0 + warp; rb < r1; rb += ROWS * kWarps) {
+        double s[ROWS];
+        float t[ROWS];
+        uint32_t m[ROWS];
+#pragma unroll
+        for (int u = 0; u < ROWS; ++u) {
+            s[u] = 0.0;
+            t[u] = 0.f;
+            m[u] = kFull;
+        }
         if (VEC) {
-#pragma unroll 4
+#pragma unroll(ROWS == 1 ? 4 : 2)
             for (int c = lane * 4; c < N; c += 128) {
-                const float4 v = __ldg(reinterpret_cast<const float4*>(row + c));
-                acc1(v.x, s, t, m);
-                acc1(v.y, s, t, m);
-                acc1(v.z, s, t, m);
-                acc1(v.w, s, t, m);
+                float4 v[ROWS];
+#pragma unroll
+                for (int u = 0; u < ROWS; ++u) {
+                    const int r = rb + u * kWarps;
+                    v[u] = (r < r1) ? __ldg(reinterpret_cast<const float4*>(C + (long long)r * ldc + c))
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+#pragma unroll
+                for (int u = 0; u < ROWS; ++u) {
+                    acc1(v[u].x, s[u], t[u], m[u]);
+                    acc1(v[u].y, s[u], t[u], m[u]);
+                    acc1(v[u].z, s[u], t[u], m[u]);
+                    acc1(v[u].w, s[u], t[u], m[u]);
+                }
             }
         } else {
-#pragma unroll 4
-            for (int c = lane; c < N; c += 32) acc1(__ldg(row + c), s, t, m);
+#pragma unroll(ROWS == 1 ? 4 : 2)
+            for (int c = lane; c < N; c += 32) {
+                float v[ROWS];
+#pragma unroll
+                for (int u = 0; u < ROWS; ++u) {
+                    const int r = rb + u * kWarps;
+                    v[u] = (r < r1) ? __ldg(C + (long long)r * ldc + c) : 0.f;
+                }
+#pragma unroll
+                for (int u = 0; u < ROWS; ++u) acc1(v[u], s[u], t[u], m[u]);
+            }
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
-            s = __dadd_rn(s, __shfl_xor_sync(kFull, s, o));
-            t += __shfl_xor_sync(kFull, t, o);
-            m = min(m, __shfl_xor_sync(kFull, m, o));
+#pragma unroll
+            for (int u = 0; u < ROWS; ++u) {
+                s[u] = __dadd_rn(s[u], __shfl_xor_sync(kFull, s[u], o));
+                t[u] += __shfl_xor_sync(kFull, t[u], o);
+                m[u] = min(m[u], __shfl_xor_sync(kFull, m[u], o));
+            }
         }
-        if (lane == 0) {
-            const double d = fabs(s - expc[r]);
-            w.lact[r] = s;
-            w.ld[r] = d;
-            w.lw[r] = cert_window(s, t, m, N, d);
+        if (lane < ROWS) {
+            // lane u writes row u's results (a select keeps s, t, m in registers)
+            double su = s[0];
+            float tu = t[0];
+            uint32_t mu = m[0];
+#pragma unroll
+            for (int u = 1; u < ROWS; ++u)
+                if (lane == u) {
+                    su = s[u];
+                    tu = t[u];
+                    mu = m[u];
+                }
+            const int r = rb + lane * kWarps;
+            if (r < r1) {
+                const double d = fabs(su - expc[r]);
+                w.lact[r] = su;
+                w.ld[r] = d;
+                w.lw[r] = cert_window(su, tu, mu, N, d);
+            }
         }
     }
     fence_acq_rel_gpu();
@@ -1200,7 +1248,8 @@ int launch_encode(abft_ws* ws, const float* dA, int64_t lda, const float* dB, in
 }
 
 int launch_verify(abft_ws* ws, const float* dC, int64_t ldc, int f, double tau, int injected, int it,
-                  cudaStream_t st, int plan_it, float add_delta, int log_inj, double* calib_out) {
+                  cudaStream_t st, int plan_it, float add_delta, int log_inj, double* calib_out,
+                  unsigned long long cond) {
     const int M = ws->M_b, N = ws->counts[f];
     const float* Cf = dC + ws->offsets[f];
     if (int rc = ensure_kernel_attrs(ws->device)) return rc;
@@ -1222,7 +1271,7 @@ int launch_verify(abft_ws* ws, const float* dC, int64_t ldc, int f, double tau, 
         const int dw_in_smem = (16LL * N <= kTmaSmem) ? 1 : 0;
         k_verify_tma<<<dim3(groups, chunks), kThreads, kTmaSmem, st>>>(
             map, Cf, ldc, M, N, rows_per, groups * chunks, dw_in_smem, expv, tau, injected, f, ws->F, it, ws->d, Cw,
-            plan, plan_it, add_delta, log_inj, calib_out);
+            plan, plan_it, add_delta, log_inj, calib_out, cond);
         return check_launch("verify (tma)");
     }
 
@@ -1239,11 +1288,11 @@ int launch_verify(abft_ws* ws, const float* dC, int64_t ldc, int f, double tau, 
     if (vec)
         k_verify<true><<<grid, kThreads, smem, st>>>(Cf, ldc, M, N, rows_per, total, dw_in_smem, expv, tau,
                                                      injected, f, ws->F, it, ws->d, Cw, plan, plan_it, add_delta,
-                                                     log_inj, calib_out);
+                                                     log_inj, calib_out, cond);
     else
         k_verify<false><<<grid, kThreads, smem, st>>>(Cf, ldc, M, N, rows_per, total, dw_in_smem, expv, tau,
                                                       injected, f, ws->F, it, ws->d, Cw, plan, plan_it, add_delta,
-                                                      log_inj, calib_out);
+                                                      log_inj, calib_out, cond);
     return check_launch("verify");
 }
 
@@ -1251,12 +1300,14 @@ int launch_localize(abft_ws* ws, float* dC, int64_t ldc, int f, double tau, int 
                     int64_t ldg, int it, int correct_mode, cudaStream_t st, int plan_it) {
     const int M = ws->M_b, N = ws->counts[f];
     float* Cf = dC + ws->offsets[f];
-    // about 64 KB of C per CTA, whole warps of rows
+    // about 64 KB of C per CTA, but no more rows than give two CTAs per SM
+    // (whole warps of rows, 8 to 256 rows)
     long long rows = 65536 / ((long long)N * 4);
+    rows = std::min(rows, (long long)((M + 2 * ws->sms - 1) / (2 * ws->sms)));
     if (rows < kWarps) rows = kWarps;
     if (rows > 256) rows = 256;
-    int rows_per = (int)((rows + kWarps - 1) / kWarps) * kWarps;
-    int nblocks = (M + rows_per - 1) / rows_per;
+    const int rows_per = (int)((rows + kWarps - 1) / kWarps) * kWarps;
+    const int nblocks = (M + rows_per - 1) / rows_per;
     const bool vec = aligned16(Cf) && (ldc % 4 == 0) && (N % 4 == 0);
     const double* expc = ws->d.expCol + (long long)f * M;
     if (it >= ws->max_iters) it = -1;
@@ -1266,14 +1317,16 @@ int launch_localize(abft_ws* ws, float* dC, int64_t ldc, int f, double tau, int 
         set_error("drain correction needs a workspace with max_iters > iteration index");
         return ABFT_ERR_ARG;
     }
-    if (vec)
-        k_localize<true><<<nblocks, kThreads, 0, st>>>(Cf, ldc, M, N, rows_per, nblocks, expc, tau, injected, dG,
-                                                       ldg, ws->offsets[f], f, ws->F, it, drain, cap, ws->d,
-                                                       plan_it >= 0 ? ws->d.plan : nullptr, plan_it);
-    else
-        k_localize<false><<<nblocks, kThreads, 0, st>>>(Cf, ldc, M, N, rows_per, nblocks, expc, tau, injected, dG,
-                                                        ldg, ws->offsets[f], f, ws->F, it, drain, cap, ws->d,
-                                                        plan_it >= 0 ? ws->d.plan : nullptr, plan_it);
+    const InjectPlan* plan = plan_it >= 0 ? ws->d.plan : nullptr;
+#define ABFT_LOCALIZE_LAUNCH(V, R)                                                                               \
+    k_localize<V, R><<<nblocks, kThreads, 0, st>>>(Cf, ldc, M, N, rows_per, nblocks, expc, tau, injected, dG, ldg, \
+                                                   ws->offsets[f], f, ws->F, it, drain, cap, ws->d, plan, plan_it)
+    const bool narrow = N <= kLocNarrow;
+    if (vec && narrow) ABFT_LOCALIZE_LAUNCH(true, 4);
+    else if (vec) ABFT_LOCALIZE_LAUNCH(true, 1);
+    else if (narrow) ABFT_LOCALIZE_LAUNCH(false, 4);
+    else ABFT_LOCALIZE_LAUNCH(false, 1);
+#undef ABFT_LOCALIZE_LAUNCH
     return check_launch("localize");
 }
 
@@ -1400,10 +1453,10 @@ int launch_verify_static(const float* Cf, int64_t ldc, int M, int N, const doubl
     const int total = groups * chunks;
     if (vec)
         k_verify<true><<<grid, kThreads, smem, st>>>(Cf, ldc, M, N, rows_per, total, 1, expv, tau, injected, 0, 1,
-                                                     -1, w, nullptr, nullptr, 0, 0.f, 0, nullptr);
+                                                     -1, w, nullptr, nullptr, 0, 0.f, 0, nullptr, 0);
     else
         k_verify<false><<<grid, kThreads, smem, st>>>(Cf, ldc, M, N, rows_per, total, 1, expv, tau, injected, 0, 1,
-                                                      -1, w, nullptr, nullptr, 0, 0.f, 0, nullptr);
+                                                      -1, w, nullptr, nullptr, 0, 0.f, 0, nullptr, 0);
     if (int rc = check_launch("verify (static scratch)")) return rc;
     k_static_copyout<<<1, 32, 0, st>>>(w.rec, w.ctr, errcol, rowdiff, cm);
     return check_launch("verify copy-out");

@@ -63,6 +63,9 @@ struct abft_session {
     // fragments ready for the host
     cudaStream_t xfer = nullptr;
     cudaEvent_t a_in = nullptr, xjoin = nullptr;
+    // graph mode: stream on which the bodies of the conditional localisation
+    // nodes are captured
+    cudaStream_t body = nullptr;
     std::vector<cudaEvent_t> b_in, c_out;
 };
 
@@ -119,6 +122,48 @@ struct IoHooks {
     const cudaEvent_t* out_ready;  // null: no per-fragment signal
 };
 
+// Graph mode: a conditional handle of the graph being captured on st, reset
+// to 0 at every launch of the instantiated graph.
+int cond_handle(cudaStream_t st, cudaGraphConditionalHandle* h) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaGraph_t g = nullptr;
+    CK(cudaStreamGetCaptureInfo(st, &cs, nullptr, &g, nullptr, nullptr));
+    if (cs != cudaStreamCaptureStatusActive || g == nullptr) {
+        set_error("conditional localisation: stream is not capturing");
+        return ABFT_ERR_STATE;
+    }
+    CK(cudaGraphConditionalHandleCreate(h, g, 0, cudaGraphCondAssignDefault));
+    return ABFT_OK;
+}
+
+// Appends to st's capture an IF node on h (after all st has captured so far),
+// continues st's capture after it, and captures `fill` into its body on the
+// session's body stream.
+template <class Fill>
+int capture_if(abft_session* s, cudaStream_t st, cudaGraphConditionalHandle h, Fill fill) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaGraph_t g = nullptr;
+    const cudaGraphNode_t* deps = nullptr;
+    size_t nd = 0;
+    CK(cudaStreamGetCaptureInfo(st, &cs, nullptr, &g, &deps, &nd));
+    cudaGraphNodeParams p{};
+    p.type = cudaGraphNodeTypeConditional;
+    p.conditional.handle = h;
+    p.conditional.type = cudaGraphCondTypeIf;
+    p.conditional.size = 1;
+    cudaGraphNode_t node = nullptr;
+    CK(cudaGraphAddNode(&node, g, deps, nd, &p));
+    cudaGraph_t body = p.conditional.phGraph_out[0];
+    CK(cudaStreamUpdateCaptureDependencies(st, &node, 1, cudaStreamSetCaptureDependencies));
+    CK(cudaStreamBeginCaptureToGraph(s->body, body, nullptr, nullptr, 0, cudaStreamCaptureModeThreadLocal));
+    const int rc = fill(s->body);
+    cudaGraph_t out = nullptr;
+    const cudaError_t e = cudaStreamEndCapture(s->body, &out);
+    if (rc != ABFT_OK) return rc;
+    CK(e);
+    return ABFT_OK;
+}
+
 // Enqueue `repeats` protected iterations on the two streams (no host sync).
 // graph = true: the injection is read from the device plan table by the verify
 // kernel (capturable, the same graph serves every trial).
@@ -153,17 +198,28 @@ int enqueue_loop(abft_session* s, const abft_online_args* a, const std::vector<P
             CK(cudaStreamWaitEvent(s->verify, s->compute_done[f], 0));
             const bool prof = !graph && s->profile && (size_t)(2 * nv + 1) < s->vprof.size();
             if (prof) CK(cudaEventRecord(s->vprof[2 * nv], s->verify));
+            // Graph mode: fragment f's localisation sits in a conditional node
+            // that the verify kernel opens only when it detected a column, so
+            // clean fragments cost no launch (host-enqueued, the localisation
+            // kernel is launched and returns at once when nothing was found).
+            cudaGraphConditionalHandle h = 0;
+            if (graph && do_localize) RC(cond_handle(s->verify, &h));
             if (graph)
                 RC(launch_verify(s->ws, dC, s->ldc, f, s->tau[f], 0, log_it, s->verify, it, a->add_delta,
-                                 (a->log && inject_on) ? 1 : 0));
+                                 (a->log && inject_on) ? 1 : 0, nullptr, h));
             else
                 RC(launch_verify(s->ws, dC, s->ldc, f, s->tau[f], injected, log_it, s->verify));
             if (prof) CK(cudaEventRecord(s->vprof[2 * nv + 1], s->verify));
             ++nl;
             ++nv;
-            if (do_localize) {
+            if (do_localize && graph) {
+                RC(capture_if(s, s->verify, h, [&](cudaStream_t bs) {
+                    return launch_localize(s->ws, dC, s->ldc, f, s->tau[f], injected, s->dG, s->ldg, it,
+                                           a->correct_mode, bs, it);
+                }));
+            } else if (do_localize) {
                 RC(launch_localize(s->ws, dC, s->ldc, f, s->tau[f], injected, s->dG, s->ldg, it, a->correct_mode,
-                                   s->verify, graph ? it : -1));
+                                   s->verify, -1));
                 ++nl;
             }
             if (io && io->out_ready && it == a->repeats - 1) CK(cudaEventRecord(io->out_ready[f], s->verify));
@@ -361,6 +417,7 @@ int abft_session_create(const abft_session_cfg* c, abft_session** out) {
         if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s->c_out[f], cudaEventDisableTiming);
     }
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&s->xfer, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&s->body, cudaStreamNonBlocking);
     if (e != cudaSuccess) return fail(cuda_fail(e, "event create"));
     int rc = abft_ws_create(s->M_b, s->N_b, s->K, s->F, c->counts, c->offsets, c->max_iters, nullptr, 0, &s->ws);
     if (rc != ABFT_OK) return fail(rc);
@@ -391,6 +448,7 @@ int abft_session_destroy(abft_session* s) {
     for (auto e : s->c_out)
         if (e) cudaEventDestroy(e);
     if (s->xfer) cudaStreamDestroy(s->xfer);
+    if (s->body) cudaStreamDestroy(s->body);
     if (s->handle) cublasDestroy(s->handle);
     if (s->compute) cudaStreamDestroy(s->compute);
     if (s->verify) cudaStreamDestroy(s->verify);
@@ -533,6 +591,8 @@ int abft_session_online(abft_session* s, const abft_online_args* a, abft_online_
     r->device_ms = ms;
     r->host_ms = std::chrono::duration<double, std::milli>(h1 - h0).count();
     RC(abft_ws_read_counters(s->ws, r->cm, &r->n_restored));
+    // graph mode: one localisation kernel ran per detected fragment (TP + FP)
+    if (a->graph && (a->mode == ABFT_INJECT_ADD || a->mode == ABFT_INJECT_SWIFI)) nl += r->cm[0] + r->cm[2];
     r->kernel_launches = nl;
     r->verify_launches = nv;
     prof_stats(s, nv, r);

@@ -178,6 +178,10 @@ def test_graph_mode_matches_oracle(mode, zone, correct, kernel, abft, orc):
         o = orc.online_loop(C0, A, B, counts, offsets, tau, mode, zone, 1.0e6, base, 0, 12,
                             golden=C0 if mode == "swifi" else None)
         compare(s, res, o, 12)
+        # localisation runs (as a conditional graph node) only for detected fragments
+        detected = res["cm"][0] + res["cm"][2] if mode != "none" else 0
+        drain_kernel = 1 if (mode != "none" and correct == "drain") else 0
+        assert res["kernel_launches"] == 4 * 12 + detected + drain_kernel
     s.close()
     abft.set_verify_kernel("auto")
 
