@@ -16,8 +16,11 @@
 // bit ("certified"). Otherwise S differs from it by at most 2*gamma_n*T and
 // the decision logic carries that window: a column whose window cannot reach
 // the threshold or the current maximum is decided without it; the few that
-// can are re-summed sequentially in the reference's order. The arg-max is then
-// the reference's own 256-slot strided scan and tree on exact values.
+// can are re-summed in the reference's order (exact_chain, which proves runs
+// of terms exact or absorbed and steps through the rest). The arg-max is then
+// the reference's own 256-slot strided scan and tree on exact values. A
+// second verify body (k_verify_tma) stages the tile through shared memory
+// with bulk tensor copies; the localisation kernel certifies row sums alike.
 //
 // Encode kernels (colSumA, expectedRow, rowSumB_f, expectedCol_f) are
 // sequential chains by definition; they run one chain per thread fed from

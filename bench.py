@@ -10,10 +10,15 @@ iteration, detection threshold 1e-5*K*max|A|*max|B|. One step = one trial of
 broadcast from rank 0 over NCCL before timing.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--verify-kernel auto|ldg|tma] [--timeline TRACE_JSON]
 
 Rank 0 prints one JSON line. `value` is whole-job protected TFLOP/s
-(2*M*N*K*iterations / max-over-ranks device time). `--impl reference` times
-the reference's algorithm on the host cores (CPU oracle + BLAS SGEMM).
+(2*M*N*K*iterations / max-over-ranks device time); `e2e` the same through
+host buffers (copies timed); `roofline` the verify kernel against the
+measured HBM copy bandwidth; `cpu_baseline` the protected iterations on the
+host cores. `--impl reference` times the reference's algorithm on the host
+cores (CPU oracle + BLAS SGEMM). `--timeline` adds a CUPTI kernel timeline
+of one protected trial and the ABFT kernels' overlap with the SGEMMs.
 """
 import argparse
 import importlib
