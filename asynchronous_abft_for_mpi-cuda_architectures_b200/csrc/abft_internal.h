@@ -125,6 +125,8 @@ int launch_inject(float* dC, int64_t ldc, int row, int col, int mode, float delt
                   int frag, cudaStream_t st);
 // Selects the verify body (ABFT_VERIFY_*); returns the previous setting or -1.
 int set_verify_kernel(int which);
+// The current selection (ABFT_VERIFY_*).
+int verify_kernel();
 int launch_verify_static(const float* Cf, int64_t ldc, int M, int N, const double* expv, double tau, int injected,
                          int* errcol, double* rowdiff, int* cm, cudaStream_t st);
 

@@ -1425,6 +1425,8 @@ int set_verify_kernel(int which) {
     return g_verify_kernel.exchange(which);
 }
 
+int verify_kernel() { return g_verify_kernel.load(std::memory_order_relaxed); }
+
 int launch_verify_static(const float* Cf, int64_t ldc, int M, int N, const double* expv, double tau, int injected,
                          int* errcol, double* rowdiff, int* cm, cudaStream_t st) {
     if (N > kStaticMaxCols) {

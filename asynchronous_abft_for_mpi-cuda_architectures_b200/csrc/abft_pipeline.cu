@@ -55,6 +55,7 @@ struct abft_session {
     // graph mode: one captured loop, replayed while its shape stays the same
     cudaGraphExec_t gexec = nullptr;
     int g_repeats = -1, g_mode = -1, g_correct = -1, g_log = -1, g_launches = 0, g_vlaunches = 0;
+    int g_vkernel = -1;  // verify body selection the graph was captured with
     float g_delta = 0.f;
     InjectPlan* plan_host = nullptr;  // pinned, max_iters entries
     cudaGraphExec_t bexec = nullptr;  // graph of the baseline pass
@@ -257,11 +258,11 @@ void drop_graph(abft_session* s) {
 }
 
 // Capture the loop once for this shape (repeats, mode, correction, logging,
-// fault size); thresholds and the golden pointer are baked in, so setting
-// them drops the graph.
+// fault size, verify body selection); thresholds and the golden pointer are
+// baked in, so setting them drops the graph.
 int build_graph(abft_session* s, const abft_online_args* a, const std::vector<Plan>& plan) {
     if (s->gexec && s->g_repeats == a->repeats && s->g_mode == a->mode && s->g_correct == a->correct_mode &&
-        s->g_log == a->log && s->g_delta == a->add_delta)
+        s->g_log == a->log && s->g_delta == a->add_delta && s->g_vkernel == verify_kernel())
         return ABFT_OK;
     drop_graph(s);
     CK(cudaStreamBeginCapture(s->compute, cudaStreamCaptureModeThreadLocal));
@@ -294,6 +295,7 @@ int build_graph(abft_session* s, const abft_online_args* a, const std::vector<Pl
     s->g_correct = a->correct_mode;
     s->g_log = a->log;
     s->g_delta = a->add_delta;
+    s->g_vkernel = verify_kernel();
     s->g_launches = nl;
     s->g_vlaunches = nv;
     return ABFT_OK;
