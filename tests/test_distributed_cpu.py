@@ -1,5 +1,5 @@
 """Multi-rank plumbing on CPU (gloo): panel distribution over the Pr x Pc grid
-and the metric reductions, with world sizes 2 and 4."""
+and the metric reductions, with world sizes 2, 4 and 8 (grids 1x2, 2x2, 2x4)."""
 import os
 import socket
 
@@ -48,7 +48,7 @@ def worker(rank, world, port, M, K, N, q):
         q.put((rank, False, repr(e), None, None))
 
 
-@pytest.mark.parametrize("world,shape", [(2, (300, 40, 517)), (4, (301, 33, 250))])
+@pytest.mark.parametrize("world,shape", [(2, (300, 40, 517)), (4, (301, 33, 250)), (8, (257, 17, 130))])
 def test_panels_and_reductions(world, shape):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
