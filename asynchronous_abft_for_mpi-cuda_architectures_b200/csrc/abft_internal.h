@@ -51,7 +51,7 @@ struct Counters {
     int cm[4];       // TP, TN, FP, FN
     int n_restored;
     int n_pending;
-    int fault;  // a verify kernel's bounded wait for a bulk copy ran out
+    int fault;  // a verify kernel's bounded wait for a bulk copy ran out (or its ring was misplaced)
     int pad;
 };
 

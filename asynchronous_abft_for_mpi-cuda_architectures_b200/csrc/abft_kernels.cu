@@ -56,6 +56,7 @@ constexpr int kTmaRows = 32;
 constexpr int kTmaStages = 6;
 constexpr int kStageBytes = kTmaRows * kGroupCols * 4;
 constexpr int kTmaSmem = kTmaStages * kStageBytes;
+constexpr int kTmaAlign = 1024;  // alignment of the ring (bulk tensor copy destinations)
 // Fragments of at least this many bytes use the TMA body by default: measured on
 // B200 with L2 emptied before each launch, the two bodies are within 1 us of
 // each other up to 268 MB (128-bit loads ahead by 2-8 %), TMA ahead by 2 % at 1 GiB.
@@ -651,9 +652,14 @@ __global__ void __launch_bounds__(kThreads, 2)
                  int rows_per, int total_ctas, int dw_in_smem, const double* __restrict__ expv, double tau,
                  int injected, int f, int F, int it, WsDev w, float* Cw, const InjectPlan* __restrict__ plan,
                  int plan_it, float add_delta, int log_inj, double* calib_out, cudaGraphConditionalHandle cond) {
-    extern __shared__ __align__(1024) unsigned char ring[];
+    // The dynamic shared memory is launched kTmaAlign bytes larger than the
+    // ring and the ring starts at the first kTmaAlign boundary in it: where
+    // the dynamic area begins depends on the static shared memory before it
+    // and on how the kernel was compiled, and the copies need the alignment.
+    extern __shared__ __align__(16) unsigned char ring_raw[];
     __shared__ SelectSmem sel;
     __shared__ __align__(8) uint64_t full[kTmaStages];
+    unsigned char* const ring = ring_raw + ((kTmaAlign - (smem_addr(ring_raw) & (kTmaAlign - 1))) & (kTmaAlign - 1));
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = blockIdx.x, chunk = blockIdx.y;
@@ -661,7 +667,10 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int c0 = gc0 + lane * 4;
     const int r0 = chunk * rows_per;
     const int r1 = min(M, r0 + rows_per);
-    const int nst = (r1 - r0 + kTmaRows - 1) / kTmaRows;
+    // (cannot fail: keeps a misplaced ring from ever reaching a copy)
+    const bool ring_ok = (smem_addr(ring) & (kTmaAlign - 1)) == 0;
+    const int nst = ring_ok ? (r1 - r0 + kTmaRows - 1) / kTmaRows : 0;
+    if (!ring_ok && tid == 0) atomicOr(&w.ctr->fault, 1);
 
     if (tid == 0) {
 #pragma unroll
@@ -1202,7 +1211,7 @@ int ensure_kernel_attrs(int device) {
     set((const void*)k_colchain<true, false>, kColSmem);
     set((const void*)k_verify<true>, kVerifySmemMax);
     set((const void*)k_verify<false>, kVerifySmemMax);
-    set((const void*)k_verify_tma, kTmaSmem);
+    set((const void*)k_verify_tma, kTmaSmem + kTmaAlign);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
     done.insert(device);
     return ABFT_OK;
@@ -1269,10 +1278,10 @@ int launch_verify(abft_ws* ws, const float* dC, int64_t ldc, int f, double tau, 
     const bool want_tma = (choice == 2) || (choice == 0 && 4LL * M * N >= kTmaMinBytes);
     CUtensorMap map;
     if (tma_ok && want_tma && fragment_tensor_map(&map, Cf, ldc, M, N)) {
-        const int per_sm = resident_per_sm((const void*)k_verify_tma, kTmaSmem);
+        const int per_sm = resident_per_sm((const void*)k_verify_tma, kTmaSmem + kTmaAlign);
         verify_geometry_tma(per_sm * ws->sms, M, N, groups, chunks, rows_per);
         const int dw_in_smem = (16LL * N <= kTmaSmem) ? 1 : 0;
-        k_verify_tma<<<dim3(groups, chunks), kThreads, kTmaSmem, st>>>(
+        k_verify_tma<<<dim3(groups, chunks), kThreads, kTmaSmem + kTmaAlign, st>>>(
             map, Cf, ldc, M, N, rows_per, groups * chunks, dw_in_smem, expv, tau, injected, f, ws->F, it, ws->d, Cw,
             plan, plan_it, add_delta, log_inj, calib_out, cond);
         return check_launch("verify (tma)");
