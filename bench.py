@@ -226,7 +226,11 @@ class ColdL2:
 
 
 def isolated_verify_ms(abft, torch, s, reps=3):
-    """Average time of one verify launch alone on a cold buffer (L2 emptied before each)."""
+    """Average time of one verify launch alone on a cold buffer (L2 emptied
+    before each): the mean over every launch. CUDA event timestamps advance in
+    steps of about 2 us on B200, so a single interval is quantised; the start of
+    each interval falls at an arbitrary point between steps, which makes the
+    mean of many intervals unbiased where their median is not."""
     ws = s.ws_handle
     st = torch.cuda.Stream(device=s.device)
     cold = ColdL2(torch, s.device)
@@ -244,13 +248,13 @@ def isolated_verify_ms(abft, torch, s, reps=3):
                     e1.synchronize()
                     times.append(e0.elapsed_time(e1))
     del cold
-    return statistics.median(times)
+    return statistics.mean(times)
 
 
-def isolated_localize_ms(abft, torch, s, reps=5):
+def isolated_localize_ms(abft, torch, s, reps=16):
     """One full localisation pass (row sums of a fragment that holds a planted
     fault, the row arg-max and the correction) timed alone with CUDA events on
-    its stream, L2 emptied before each launch: median ms. The loop runs inside
+    its stream, L2 emptied before each launch: mean ms. The loop runs inside
     the NVTX range "isolated_localize" (a target for ncu --nvtx-include)."""
     ws = s.ws_handle
     st = torch.cuda.Stream(device=s.device)
@@ -274,12 +278,12 @@ def isolated_localize_ms(abft, torch, s, reps=5):
             times.append(e0.elapsed_time(e1))
     torch.cuda.nvtx.range_pop()
     del cold
-    return statistics.median(times)
+    return statistics.mean(times)
 
 
-def isolated_verify_large(abft, torch, device, M=16384, N=4096, reps=5):
+def isolated_verify_large(abft, torch, device, M=16384, N=4096, reps=9):
     """The same verify kernel alone on one large fragment (M x N floats), L2
-    emptied before each launch: (bytes per launch, median ms)."""
+    emptied before each launch: (bytes per launch, mean ms)."""
     C = torch.randn((M, N), dtype=torch.float32, device=device)
     ws = abft.kernels.Workspace(M, N, 1, [N], [0])
     st = torch.cuda.Stream(device=device)
@@ -296,7 +300,7 @@ def isolated_verify_large(abft, torch, device, M=16384, N=4096, reps=5):
             times.append(e0.elapsed_time(e1))
     ws.close()
     del C, cold
-    return 4.0 * M * N + 24.0 * N, statistics.median(times)
+    return 4.0 * M * N + 24.0 * N, statistics.mean(times)
 
 
 def overlap_timeline(torch, s, args, base, rank, path):
@@ -485,7 +489,8 @@ def run_ours(args):
                 "bytes_per_launch": bytes_launch, "launch_ms": v_avg_max[1],
                 "timing": "CUDA events on the launching stream around each launch, kernel alone, "
                           "L2 emptied before each launch (256 MiB written, then 256 MiB read so no dirty "
-                          "lines are written back during the launch), median",
+                          "lines are written back during the launch), mean of 24 launches (event timestamps "
+                          "advance in ~2 us steps; the mean of many intervals is unbiased, their median is not)",
                 "live": {"achieved": live_gbs, "frac": (live_gbs / peak) if live_gbs else None,
                          "launch_ms": v_avg_max[0],
                          "note": "inside the protected loop on the low-priority verify stream: the kernel "
