@@ -82,7 +82,8 @@ void print_help() {
         "  --relative-threshold R         tau = R * K * max|A| * max|B|\n"
         "  --correct {inloop|drain}       correct inside the loop or after it\n"
         "  --verify-priority {low|default|high}\n"
-        "  --csv-extra                    append encode/verify columns to the CSV\n"
+        "  --csv-extra                    append run-setting columns, encode_ms and the corrected C's\n"
+        "                                 max relative error against the fault-free SGEMM to the CSV\n"
         "  --graph                        replay each trial's loop as a CUDA graph\n"
         "  --inject-seed-mode {reference|json}  json: (i,j) uniform over the tile from seed 1 + iteration\n"
         "  --help                         this message\n";
@@ -257,6 +258,7 @@ int main(int argc, char** argv) {
 
     std::vector<float> A_stripe((size_t)M_b * K), B_stripe((size_t)K * N_b);
     std::vector<double> tau(F, 0.0);
+    double last_encode_ms = 0.0;
 
     // regen_inputs (main.cu:126-165): rank 0 draws the full matrices; stripes
     // travel device to device (rank 0 -> (pr,0) / (0,pc), then a broadcast
@@ -311,6 +313,7 @@ int main(int argc, char** argv) {
         ABFT_TRY(abft_session_set_tau(sess, tau.data()));
         double enc_ms = 0;
         ABFT_TRY(abft_session_encode(sess, &enc_ms));
+        last_encode_ms = enc_ms;
         return 0;
     };
     if (int r = regen(cfg.seed_a, cfg.seed_b)) return r;
@@ -323,6 +326,10 @@ int main(int argc, char** argv) {
     const int mode = cfg.inject == "add" ? ABFT_INJECT_ADD : (cfg.inject == "swifi" ? ABFT_INJECT_SWIFI : ABFT_INJECT_NONE);
 
     std::vector<double> base_samples, prot_samples;
+    // --csv-extra: the last trial's fault-free C (its own baseline pass), to
+    // measure how far the protected run's final buffers are from it.
+    const bool check_corrected = cfg.csv_extra && !cfg.baseline_only && !cfg.calibrate;
+    std::vector<float> clean_c;
     int cm_local[4] = {0, 0, 0, 0};
     int restored_local = 0;
     bool golden_set = false;
@@ -363,6 +370,10 @@ int main(int argc, char** argv) {
         double bdev = 0, bhost = 0;
         ABFT_TRY(abft_session_baseline(sess, cfg.repeats, cfg.graph ? 1 : 0, &bdev, &bhost));
         if (record) base_samples.push_back(bhost / cfg.repeats);
+        if (check_corrected && t == TOTAL - 1) {
+            clean_c.resize((size_t)M_b * N_b);
+            CUDA_TRY(cudaMemcpy(clean_c.data(), dC0, sizeof(float) * clean_c.size(), cudaMemcpyDeviceToHost));
+        }
         // Golden capture (main.cu:217-226). The reference uploads it to the
         // device only once (pipeline/passes.cuh:110-116), so only the first
         // capture is used; the same holds here.
@@ -405,6 +416,27 @@ int main(int argc, char** argv) {
     if (world_rank == 0 && !cfg.baseline_only && !cfg.calibrate)
         std::cout << "[Rank 0] " << NUM_TRIALS << " timed trials x " << cfg.repeats << " iters/trial"
                   << (cfg.reseed_per_trial ? "  (fresh A,B per trial)" : "") << "\n";
+
+    // Corrected C against the fault-free SGEMM: max |C - C_clean| / max |C_clean|
+    // over the buffers that hold the last trial's final iterations (both slots
+    // once there were two iterations), max over ranks; NaN if a final buffer
+    // holds a NaN where the clean C does not.
+    double corr_err[3] = {0.0, 0.0, 0.0};  // max |diff|, max |clean|, NaN seen
+    if (check_corrected && !clean_c.empty()) {
+        std::vector<float> fin(clean_c.size());
+        for (int slot = 0; slot < std::min(cfg.repeats, 2); ++slot) {
+            CUDA_TRY(cudaMemcpy(fin.data(), slot == 0 ? dC0 : dC1, sizeof(float) * fin.size(),
+                                cudaMemcpyDeviceToHost));
+            for (size_t i = 0; i < fin.size(); ++i) {
+                const double g = clean_c[i];
+                const double d = std::fabs((double)fin[i] - g);
+                if (std::isnan(d)) corr_err[2] = 1.0;
+                else corr_err[0] = std::max(corr_err[0], d);
+                if (!std::isnan(g)) corr_err[1] = std::max(corr_err[1], std::fabs(g));
+            }
+        }
+        COMM_TRY(comm_allreduce_double_max(comm, corr_err, 3));
+    }
 
     abft_timing bl{}, pl{};
     ABFT_TRY(abft_stats_of(base_samples.data(), (int)base_samples.size(), &bl));
@@ -468,10 +500,19 @@ int main(int argc, char** argv) {
         abft_metrics_report(&m, buf.data(), buf.size());
         std::cout << buf.data() << std::flush;
         if (cfg.csv_extra) {
-            const std::string eh = "correct_mode,verify_priority,dist,add_delta";
+            double rel = 0.0;
+            if (corr_err[2] != 0.0) rel = NAN;
+            else if (corr_err[1] > 0.0) rel = corr_err[0] / corr_err[1];
+            if (check_corrected)
+                std::cout << "Corrected C vs fault-free: max|C - C_clean| / max|C_clean| = " << std::scientific
+                          << std::setprecision(3) << rel << std::defaultfloat << "\n";
+            char relbuf[32];
+            std::snprintf(relbuf, sizeof(relbuf), "%.6e", rel);
+            const std::string eh = "correct_mode,verify_priority,dist,add_delta,encode_ms,corrected_max_rel_err";
             const std::string ev = std::string(cfg.correct_mode == ABFT_CORRECT_DRAIN ? "drain" : "inloop") + "," +
                                    std::to_string(cfg.verify_priority) + "," + (cfg.dist ? "normal" : "uniform") +
-                                   "," + std::to_string(cfg.add_delta);
+                                   "," + std::to_string(cfg.add_delta) + "," + std::to_string(last_encode_ms) + "," +
+                                   (check_corrected ? std::string(relbuf) : std::string(""));
             ABFT_TRY(abft_metrics_csv_append(&m, cfg.csv_path.c_str(), eh.c_str(), ev.c_str()));
         } else {
             ABFT_TRY(abft_metrics_csv_append(&m, cfg.csv_path.c_str(), nullptr, nullptr));
