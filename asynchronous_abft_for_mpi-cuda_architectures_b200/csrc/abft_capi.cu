@@ -151,6 +151,10 @@ int abft_ws_create(int M_b, int N_b, int K, int F, const int* counts, const int*
     }
     char* b = static_cast<char*>(ws->base);
     e = cudaMemset(b + L.vacc_m, 0xff, sizeof(uint32_t) * ws->nfpad);
+    // The clears run on the legacy default stream and do not block the host;
+    // callers launch on their own (possibly non-blocking) streams, which are
+    // not ordered after them, so they must be complete before returning.
+    if (e == cudaSuccess) e = cudaStreamSynchronize(nullptr);
     if (e != cudaSuccess) {
         if (ws->owns) cudaFree(ws->base);
         delete ws;

@@ -120,6 +120,13 @@ int abft_ws_read_checksums(abft_ws* ws, double* colSumA, double* expRow, double*
 
 /* ------------------------------------------------------------------------
  * Kernels (enqueue only, on the caller's stream).
+ *
+ * Calls that share a workspace must run one after another on the GPU (one
+ * stream, or streams ordered by events): verify and localise keep their
+ * per-column / per-row accumulators and arrival counters in the workspace and
+ * leave them cleared for the next launch, as the reference's single verify
+ * stream does with its shared scratch (pipeline/buffers.cuh:24-27). Separate
+ * workspaces are independent.
  * ---------------------------------------------------------------------- */
 
 /* Checksum encoding of one rank tile, all fragments:

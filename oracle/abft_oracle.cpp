@@ -2,7 +2,7 @@
 //
 // TEST INFRASTRUCTURE ONLY. Nothing in the product links, loads or calls this
 // file: tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg use it
-// as the checker (and as the timed CPU arm), nothing else.
+// as the reference of correctness (and as the timed CPU arm), nothing else.
 //
 // Every function restates one piece of FaridRojas/Asynchronous_ABFT_for_MPI-
 // CUDA_Architectures in the reference's own evaluation order, so that results

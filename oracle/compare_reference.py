@@ -3,7 +3,7 @@ built for sm_100a, one rank) and this project's abft_gemm with identical flags
 on the single-GPU workloads, and print a markdown table of GFLOPS, overhead and
 the confusion matrix of each.
 
-TEST / BASELINE INFRASTRUCTURE ONLY. Needs a GPU.
+MEASUREMENT INFRASTRUCTURE ONLY (not part of the product). Needs a GPU.
 
     python oracle/compare_reference.py [--quick] > table.md
 """

@@ -1,6 +1,6 @@
 """CPU baseline of the protected SGEMM: the reference's algorithm on host cores.
 
-TEST / BASELINE INFRASTRUCTURE ONLY: bench.py's CPU-baseline leg and its
+TEST AND CPU-BASELINE INFRASTRUCTURE ONLY: bench.py's CPU-baseline leg and its
 `--impl reference` arm call this; the product never does. One protected
 iteration = the SGEMM of the rank tile (numpy/BLAS, all host threads) followed
 by the reference's verification exactly as pass_online_loop runs it

@@ -1,8 +1,9 @@
 """ctypes/numpy front end of the CPU oracle (oracle/abft_oracle.cpp).
 
-TEST INFRASTRUCTURE ONLY (the checker, and the timed CPU arm of bench.py). The
-arithmetic lives in the C++ file, which restates the reference's kernels in the
-reference's evaluation order; this module only marshals numpy arrays.
+TEST INFRASTRUCTURE ONLY (the tests' reference of correctness, and the timed
+CPU arm of bench.py). The arithmetic lives in the C++ file, which restates the
+reference's kernels in the reference's evaluation order; this module only
+marshals numpy arrays.
 """
 import ctypes
 import os
