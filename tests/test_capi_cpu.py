@@ -85,3 +85,53 @@ def test_verify_kernel_selector(abft):
     assert "abft_set_verify_kernel" in abft._lib.last_error()
     with pytest.raises(KeyError):
         abft.set_verify_kernel("fast")
+
+
+def test_device_entry_points_reject_bad_arguments(abft):
+    """Every device-side entry point validates its arguments before touching
+    CUDA and reports ABFT_ERR_ARG with a message (the reference aborted the
+    job instead; core/common.cuh:22-50). Only argument checks run here."""
+    lib = abft.lib
+    ERR = abft._lib.ABFT_ERR_ARG
+    fake = ctypes.c_void_p(256)  # never dereferenced: each call fails its checks first
+    out = ctypes.c_void_p()
+    i4 = (ctypes.c_int * 4)(4, 4, 4, 4)
+    o4 = (ctypes.c_int * 4)(0, 4, 8, 12)
+    cases = [
+        ("abft_ws_create", (0, 16, 8, 4, i4, o4, 1, None, 0, ctypes.byref(out))),      # M_b < 1
+        ("abft_ws_create", (16, 15, 8, 4, i4, o4, 1, None, 0, ctypes.byref(out))),     # fragment 3 past N_b
+        ("abft_ws_create", (16, 16, 8, 4, i4, o4, -1, None, 0, ctypes.byref(out))),    # max_iters < 0
+        ("abft_ws_create", (16, 16, 8, 0, i4, o4, 1, None, 0, ctypes.byref(out))),     # F < 1
+        ("abft_encode", (None, fake, 8, fake, 16, None)),
+        ("abft_verify", (None, fake, 16, 0, 1.0, 0, -1, None)),
+        ("abft_calibrate", (None, fake, 16, 0, fake, None)),
+        ("abft_localize_correct", (None, fake, 16, 0, 1.0, 0, None, 0, -1, 0, None)),
+        ("abft_drain", (None, fake, fake, 16, None, 0, 4, None)),
+        ("abft_verify_noalloc", (None, 16, 8, 8, fake, 1.0, 0, fake, fake, fake, None)),
+        ("abft_verify_noalloc", (fake, 4, 8, 8, fake, 1.0, 0, fake, fake, fake, None)),   # ldc < N
+        ("abft_verify_noalloc", (fake, 16, 0, 8, fake, 1.0, 0, fake, fake, fake, None)),  # M < 1
+        ("abft_inject_add", (None, 16, 0, 0, 1.0, None)),
+        ("abft_inject_add", (fake, 16, 0, 16, 1.0, None)),          # col outside the row
+        ("abft_inject_add", (fake, 16, -1, 0, 1.0, None)),
+        ("abft_inject_bitflip", (fake, 16, 0, 0, 32, None)),        # bit outside 0..31
+        ("abft_inject_bitflip", (fake, 16, 0, 0, -1, None)),
+        ("abft_sgemm", (None, fake, 8, fake, 16, fake, 16, 8, 16, 8)),
+        ("abft_session_create", (None, ctypes.byref(out))),
+        ("abft_session_online", (None, None, None)),
+        ("abft_session_baseline", (None, 1, 0, None, None)),
+        ("abft_session_set_tau", (None, None)),
+        ("abft_ws_read_counters", (None, None, None)),
+        ("abft_ws_read_log", (None, 1, None, None, None)),
+        ("abft_ws_reset_counters", (None, None)),
+    ]
+    for name, args in cases:
+        rc = getattr(lib, name)(*args)
+        assert rc == ERR, (name, rc)
+        assert abft._lib.last_error(), name
+    assert out.value is None  # no workspace or session was handed out
+    # a session configuration with a zero tile edge is refused before any CUDA call
+    cfg = abft._lib.SessionCfg(M_b=0, N_b=16, K=8, F=4, counts=i4, offsets=o4, dA=256, lda=8, dB=256, ldb=16,
+                               dC0=256, dC1=256, ldc=16, verify_priority=-1, max_iters=1)
+    assert lib.abft_session_create(ctypes.byref(cfg), ctypes.byref(out)) == ERR and out.value is None
+    assert lib.abft_ws_bytes(16, 16, 8, 4, i4, 1) > 0
+    assert lib.abft_ws_bytes(0, 16, 8, 4, i4, 1) == 0
