@@ -97,6 +97,10 @@ class OnlineSession:
 
     def _args(self, mode, zone, add_delta, base_seed, rank, repeats, correct, log, profile=False, graph=False,
               seed_scheme="reference"):
+        if correct not in ("inloop", "drain"):
+            raise ValueError(f"correct must be 'inloop' or 'drain', not {correct!r}")
+        if seed_scheme not in ("reference", "tile"):
+            raise ValueError(f"seed_scheme must be 'reference' or 'tile', not {seed_scheme!r}")
         lo, hi = host.swifi_zone_range(zone)
         a = OnlineArgs()
         a.mode = host.MODES[mode] if isinstance(mode, str) else int(mode)
@@ -136,7 +140,10 @@ class OnlineSession:
 
     def run_host(self, hA, hB, hC, mode="none", zone="any", add_delta=ADD_FAULT_DELTA, base_seed=0, rank=0,
                  repeats=1, correct="inloop", profile=False):
-        """End to end from host memory: H2D inputs, encode, protected loop, D2H result."""
+        """End to end from host memory: hA and hB are copied into this session's
+        A and B (overwriting them), then the checksums are encoded and the
+        protected loop runs; the final C lands in hC. Pinned host tensors let
+        the copies overlap the work."""
         for t in (hA, hB, hC):
             if t.is_cuda or t.dtype != torch.float32 or not t.is_contiguous():
                 raise ValueError("host tensors must be contiguous float32 CPU tensors")

@@ -135,3 +135,24 @@ def test_device_entry_points_reject_bad_arguments(abft):
     assert lib.abft_session_create(ctypes.byref(cfg), ctypes.byref(out)) == ERR and out.value is None
     assert lib.abft_ws_bytes(16, 16, 8, 4, i4, 1) > 0
     assert lib.abft_ws_bytes(0, 16, 8, 4, i4, 1) == 0
+
+
+def test_session_arguments_are_validated(abft):
+    """Online-loop options are checked on the host before any call: an unknown
+    correction mode, seed scheme or injection mode is an error."""
+    from importlib import import_module
+    OnlineSession = import_module(abft.__name__ + ".session").OnlineSession
+    ok = OnlineSession._args(None, "swifi", "exponent", 1.0, 7, 2, 5, "drain", True, graph=True, seed_scheme="tile")
+    assert (ok.mode, ok.zone_lo, ok.zone_hi, ok.correct_mode, ok.seed_scheme) == (abft.INJECT_SWIFI, 23, 30,
+                                                                                    abft.CORRECT_DRAIN, 1)
+    for bad in (dict(correct="later"), dict(seed_scheme="json")):
+        kw = dict(correct="inloop", seed_scheme="reference")
+        kw.update(bad)
+        with pytest.raises(ValueError):
+            OnlineSession._args(None, "add", "any", 1.0, 0, 0, 1, kw["correct"], False,
+                                seed_scheme=kw["seed_scheme"])
+    with pytest.raises(KeyError):
+        OnlineSession._args(None, "flip", "any", 1.0, 0, 0, 1, "inloop", False)
+    # an unknown SWIFI zone means the whole word, as in the reference (kernels/swifi.cuh:25-31)
+    z = OnlineSession._args(None, "swifi", "mantissa", 1.0, 0, 0, 1, "inloop", False)
+    assert (z.zone_lo, z.zone_hi) == (0, 31)
