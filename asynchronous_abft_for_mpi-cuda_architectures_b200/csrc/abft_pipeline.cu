@@ -104,8 +104,9 @@ int gemm_warmup(abft_session* s) {
             return rc;
         }
     }
-    CK(cudaStreamSynchronize(s->compute));
-    CK(cudaFree(buf));
+    const cudaError_t e = cudaStreamSynchronize(s->compute);
+    cudaFree(buf);
+    if (e != cudaSuccess) return cuda_fail(e, "gemm warm-up");
     return ABFT_OK;
 }
 

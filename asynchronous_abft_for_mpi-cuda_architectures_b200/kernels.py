@@ -46,7 +46,8 @@ class Workspace:
         self.nbytes = lib.abft_ws_bytes(self.M_b, self.N_b, self.K, self.F, _iptr(self.counts), self.max_iters)
         h = ctypes.c_void_p()
         self._buf = device_buffer
-        ptr, nb = (None, 0) if device_buffer is None else (device_buffer.data_ptr(), device_buffer.numel())
+        ptr, nb = ((None, 0) if device_buffer is None else
+                   (device_buffer.data_ptr(), device_buffer.numel() * device_buffer.element_size()))
         call("abft_ws_create", self.M_b, self.N_b, self.K, self.F, _iptr(self.counts), _iptr(self.offsets),
              self.max_iters, ptr, nb, ctypes.byref(h))
         self.handle = h
@@ -123,6 +124,9 @@ def localize_correct(ws, C, f, tau, injected=False, golden=None, it=-1, correct_
 
 
 def drain(ws, C0, C1, repeats, golden=None, stream=None):
+    """Post-loop correction: apply the fixes that localize_correct queued in
+    drain mode to the buffers C0 / C1 that still hold their iteration (the last
+    two of `repeats`), counting restores against golden when given."""
     gp, ldg = (None, 0) if golden is None else (golden.data_ptr(), golden.stride(0))
     call("abft_drain", ws.handle, C0.data_ptr(), C1.data_ptr(), C0.stride(0), gp, ldg, int(repeats),
          _stream(stream))

@@ -428,3 +428,46 @@ def test_exact_chain_adversarial_rows(abft, orc, torch_cuda):
             g = run_gpu_iteration(abft, torch_cuda, A, B, C, counts, offsets, [tau] * F, f, golden=C0)
             o = run_oracle_iteration(orc, A, B, C, counts, offsets, [tau] * F, f, golden=C0)
             assert_same(g, o)
+
+
+def test_caller_owned_workspace_memory(abft, orc, torch_cuda):
+    """A workspace placed in caller-owned device memory (any dtype; the size
+    counts in bytes) gives the same checksums and decisions as one that
+    allocates its own; a buffer one byte short is refused."""
+    import ctypes
+    torch = torch_cuda
+    M, K, N, F = 1024, 256, 768, 3
+    A, B = tiles(orc, M, K, N, 5, 6, "uniform")
+    counts, offsets = orc.split_dim(N, F)
+    c32 = np.ascontiguousarray(counts, np.int32)
+    need = abft.lib.abft_ws_bytes(M, N, K, F, c32.ctypes.data_as(ctypes.POINTER(ctypes.c_int)), 1)
+    assert need > 0
+    with pytest.raises(abft.AbftError):
+        abft.kernels.Workspace(M, N, K, counts, offsets, max_iters=1,
+                               device_buffer=torch.empty(need - 1, dtype=torch.uint8, device="cuda"))
+    mem = torch.empty((need + 3) // 4, dtype=torch.float32, device="cuda")
+    ws_own = abft.kernels.Workspace(M, N, K, counts, offsets, max_iters=1)
+    ws_ext = abft.kernels.Workspace(M, N, K, counts, offsets, max_iters=1, device_buffer=mem)
+    dA, dB = to_dev(torch, A), to_dev(torch, B)
+    C0 = product_f64(A, B)
+    res = []
+    for ws in (ws_own, ws_ext):
+        dC = to_dev(torch, add_fault(C0, 700, int(offsets[1]) + 9, 3.0))
+        abft.kernels.encode(ws, dA, dB)
+        ws.reset_counters()
+        for f in range(F):
+            abft.kernels.verify(ws, dC, f, 1e-5 * K, injected=(f == 1), it=0)
+            abft.kernels.localize_correct(ws, dC, f, 1e-5 * K, injected=(f == 1), it=0)
+        torch.cuda.synchronize()
+        cm, _ = ws.counters()
+        ec, er, rd = ws.read_log(1)
+        res.append((ws.read_checksums(), cm, ec, er, rd, dC.cpu().numpy()))
+    ws_own.close()
+    ws_ext.close()
+    (s0, cm0, ec0, er0, rd0, c0), (s1, cm1, ec1, er1, rd1, c1) = res
+    for a, b in zip(s0, s1):
+        assert np.array_equal(a.view(np.uint64), b.view(np.uint64))
+    assert list(cm0) == list(cm1) == [1, F - 1, 0, 0]
+    assert np.array_equal(ec0, ec1) and np.array_equal(er0, er1) and int(er0[0][1]) == 700
+    assert np.array_equal(rd0.view(np.uint64), rd1.view(np.uint64))
+    assert np.array_equal(c0.view(np.uint32), c1.view(np.uint32))
