@@ -125,7 +125,10 @@ bool parse(int argc, char** argv, Config& c, std::string& err) {
             else { err = "--correct must be inloop or drain"; return false; }
         } else if (a == "--verify-priority" && need(1)) {
             std::string m = argv[++i];
-            c.verify_priority = (m == "high") ? 1 : (m == "default" ? 0 : -1);
+            if (m == "low") c.verify_priority = -1;
+            else if (m == "default") c.verify_priority = 0;
+            else if (m == "high") c.verify_priority = 1;
+            else { err = "--verify-priority must be low, default or high"; return false; }
         } else if (a == "--csv-extra") c.csv_extra = true;
         else if (a == "--graph") c.graph = true;
         else if (a == "--inject-seed-mode" && need(1)) {
