@@ -137,6 +137,9 @@ SIGNATURES = {
     "abft_session_read_injections": (_I, [_P, _I, _IP, ctypes.POINTER(ctypes.c_float)]),
     "abft_session_run_host": (_I, [_P, _P, _P, _P, ctypes.POINTER(OnlineArgs), ctypes.POINTER(OnlineResult),
                                    _DP]),
+    "abft_session_run_host_steps": (_I, [_P, _I, ctypes.POINTER(_P), ctypes.POINTER(_P), ctypes.POINTER(_P),
+                                         ctypes.POINTER(OnlineArgs), ctypes.POINTER(_U64),
+                                         ctypes.POINTER(OnlineResult), _DP]),
     "abft_stats_of": (_I, [_DP, _I, ctypes.POINTER(Timing)]),
     "abft_metrics_finalize": (_I, [ctypes.POINTER(Metrics)]),
     "abft_metrics_report": (_I, [ctypes.POINTER(Metrics), ctypes.c_char_p, ctypes.c_size_t]),

@@ -68,6 +68,20 @@ struct abft_session {
     // nodes are captured
     cudaStream_t body = nullptr;
     std::vector<cudaEvent_t> b_in, c_out;
+    // run_host_steps: a second device copy of A and B (inputs alternate
+    // between the two), a stream for result copies, per input copy its
+    // arrival and release events, per C buffer the end of its last result
+    // copy, and pinned per-step counters
+    float* dA2 = nullptr;
+    float* dB2 = nullptr;
+    cudaStream_t xout = nullptr;
+    cudaEvent_t in_a[2] = {nullptr, nullptr};
+    std::vector<cudaEvent_t> in_b[2];
+    cudaEvent_t in_free_c[2] = {nullptr, nullptr}, in_free_v[2] = {nullptr, nullptr};
+    cudaEvent_t d2h_done[2] = {nullptr, nullptr};
+    cudaEvent_t vstep = nullptr, ojoin = nullptr;
+    Counters* ctr_host = nullptr;
+    int ctr_host_n = 0;
 };
 
 namespace {
@@ -122,6 +136,11 @@ struct IoHooks {
     cudaEvent_t a_ready;
     const cudaEvent_t* b_ready;
     const cudaEvent_t* out_ready;  // null: no per-fragment signal
+    // run_host_steps: both C buffers were used by an earlier step, so their
+    // first use here waits for that step's verification of them ...
+    bool carry_used = false;
+    // ... and, where not null, for the result copy that read them
+    const cudaEvent_t* slot_free = nullptr;
 };
 
 // Graph mode: a conditional handle of the graph being captured on st, reset
@@ -174,11 +193,16 @@ int enqueue_loop(abft_session* s, const abft_online_args* a, const std::vector<P
     const bool inject_on = (a->mode == ABFT_INJECT_ADD || a->mode == ABFT_INJECT_SWIFI);
     const bool do_localize = inject_on;
     bool used[2] = {false, false};
+    if (io && io->carry_used) used[0] = used[1] = true;
+    bool first[2] = {true, true};
     int nl = 0, nv = 0;
     for (int it = 0; it < a->repeats; ++it) {
         const int bi = it & 1;
         float* dC = s->dC[bi];
         if (used[bi]) CK(cudaStreamWaitEvent(s->compute, s->buf_done[bi], 0));
+        if (first[bi] && io && io->slot_free && io->slot_free[bi])
+            CK(cudaStreamWaitEvent(s->compute, io->slot_free[bi], 0));
+        first[bi] = false;
         const int log_it = (a->log && it < s->max_iters) ? it : -1;
         for (int f = 0; f < s->F; ++f) {
             if (io && it == 0) {
@@ -337,6 +361,36 @@ int ensure_prof_events(abft_session* s, int n_verify) {
     return ABFT_OK;
 }
 
+// Resources of run_host_steps, made on its first call: the second device
+// copy of A and B (same leading dimensions as the session's), the result-copy
+// stream, the input and result events, and n_steps pinned counter records.
+int ensure_step_resources(abft_session* s, int n_steps) {
+    // each resource is made only if missing, so a set-up that failed part way
+    // is completed by the next call (destroy releases whatever exists)
+    auto event = [](cudaEvent_t* e) { return *e ? cudaSuccess : cudaEventCreateWithFlags(e, cudaEventDisableTiming); };
+    if (!s->dA2) CK(cudaMalloc(&s->dA2, sizeof(float) * (size_t)s->lda * s->M_b));
+    if (!s->dB2) CK(cudaMalloc(&s->dB2, sizeof(float) * (size_t)s->ldb * s->K));
+    if (!s->xout) CK(cudaStreamCreateWithFlags(&s->xout, cudaStreamNonBlocking));
+    for (int q = 0; q < 2; ++q) {
+        CK(event(&s->in_a[q]));
+        CK(event(&s->in_free_c[q]));
+        CK(event(&s->in_free_v[q]));
+        CK(event(&s->d2h_done[q]));
+        if ((int)s->in_b[q].size() != s->F) s->in_b[q].assign(s->F, nullptr);
+        for (int f = 0; f < s->F; ++f) CK(event(&s->in_b[q][f]));
+    }
+    CK(event(&s->vstep));
+    CK(event(&s->ojoin));
+    if (s->ctr_host_n < n_steps) {
+        if (s->ctr_host) CK(cudaFreeHost(s->ctr_host));
+        s->ctr_host = nullptr;
+        s->ctr_host_n = 0;
+        CK(cudaMallocHost(&s->ctr_host, sizeof(Counters) * (size_t)n_steps));
+        s->ctr_host_n = n_steps;
+    }
+    return ABFT_OK;
+}
+
 void prof_stats(abft_session* s, int nv, abft_online_result* r) {
     r->verify_ms_sum = 0.0;
     r->verify_ms_max = 0.0;
@@ -437,6 +491,7 @@ int abft_session_destroy(abft_session* s) {
     if (s->compute) cudaStreamSynchronize(s->compute);
     if (s->verify) cudaStreamSynchronize(s->verify);
     if (s->xfer) cudaStreamSynchronize(s->xfer);
+    if (s->xout) cudaStreamSynchronize(s->xout);
     drop_graph(s);
     if (s->bexec) cudaGraphExecDestroy(s->bexec);
     if (s->plan_host) cudaFreeHost(s->plan_host);
@@ -452,6 +507,18 @@ int abft_session_destroy(abft_session* s) {
         if (e) cudaEventDestroy(e);
     if (s->xfer) cudaStreamDestroy(s->xfer);
     if (s->body) cudaStreamDestroy(s->body);
+    if (s->xout) cudaStreamDestroy(s->xout);
+    for (int q = 0; q < 2; ++q) {
+        for (auto e : {s->in_a[q], s->in_free_c[q], s->in_free_v[q], s->d2h_done[q]})
+            if (e) cudaEventDestroy(e);
+        for (auto e : s->in_b[q])
+            if (e) cudaEventDestroy(e);
+    }
+    for (auto e : {s->vstep, s->ojoin})
+        if (e) cudaEventDestroy(e);
+    if (s->dA2) cudaFree(s->dA2);
+    if (s->dB2) cudaFree(s->dB2);
+    if (s->ctr_host) cudaFreeHost(s->ctr_host);
     if (s->handle) cublasDestroy(s->handle);
     if (s->compute) cudaStreamDestroy(s->compute);
     if (s->verify) cudaStreamDestroy(s->verify);
@@ -718,6 +785,156 @@ int abft_session_run_host(abft_session* s, const float* hA, const float* hB, flo
         cudaStreamSynchronize(s->verify);
         cudaStreamSynchronize(s->compute);
     }
+    return rc;
+}
+
+int abft_session_run_host_steps(abft_session* s, int n_steps, const float* const* hA, const float* const* hB,
+                                float* const* hC, const abft_online_args* a, const uint64_t* base_seeds,
+                                abft_online_result* res, double* e2e_ms) {
+    if (!s || n_steps < 1 || !hA || !hB || !hC || !base_seeds || !res) {
+        set_error("abft_session_run_host_steps: NULL argument or n_steps < 1");
+        return ABFT_ERR_ARG;
+    }
+    for (int k = 0; k < n_steps; ++k) {
+        if (!hA[k] || !hB[k] || !hC[k]) {
+            set_error("abft_session_run_host_steps: NULL host buffer for step " + std::to_string(k));
+            return ABFT_ERR_ARG;
+        }
+    }
+    if (!a) {
+        set_error("abft_session_run_host_steps: NULL args");
+        return ABFT_ERR_ARG;
+    }
+    abft_online_args ak = *a;
+    ak.log = 0;
+    ak.profile = 0;
+    ak.graph = 0;
+    RC(check_args(s, &ak));
+    if (ak.repeats < 1) {
+        set_error("abft_session_run_host_steps: repeats must be >= 1");
+        return ABFT_ERR_ARG;
+    }
+    RC(ensure_step_resources(s, n_steps));
+    s->profile = 0;
+    std::vector<std::vector<Plan>> plans(n_steps);
+    for (int k = 0; k < n_steps; ++k) {
+        ak.base_seed = base_seeds[k];
+        RC(make_plan(s, &ak, plans[k]));
+    }
+    CK(cudaStreamSynchronize(s->verify));
+    CK(cudaStreamSynchronize(s->compute));
+    const bool drain = (a->mode == ABFT_INJECT_ADD || a->mode == ABFT_INJECT_SWIFI) &&
+                       a->correct_mode == ABFT_CORRECT_DRAIN;
+    const int fin = (a->repeats - 1) & 1;  // the C buffer that holds a step's result
+    float* const inA[2] = {const_cast<float*>(s->dA), s->dA2};
+    float* const inB[2] = {const_cast<float*>(s->dB), s->dB2};
+    const float* const origA = s->dA;
+    const float* const origB = s->dB;
+
+    auto run = [&]() -> int {
+        CK(cudaEventRecord(s->t0, s->compute));
+        CK(cudaStreamWaitEvent(s->xfer, s->t0, 0));
+        CK(cudaStreamWaitEvent(s->xout, s->t0, 0));
+        CK(cudaStreamWaitEvent(s->verify, s->t0, 0));
+        RC(abft_ws_reset_counters(s->ws, s->verify));
+        // inputs of step k into copy k % 2, once step k - 2 no longer reads it
+        // (its SGEMMs on the compute stream, its encode on the verify stream);
+        // B goes one fragment at a time, as in run_host
+        auto upload = [&](int k) -> int {
+            const int q = k & 1;
+            if (k >= 2) {
+                CK(cudaStreamWaitEvent(s->xfer, s->in_free_c[q], 0));
+                CK(cudaStreamWaitEvent(s->xfer, s->in_free_v[q], 0));
+            }
+            CK(cudaMemcpy2DAsync(inA[q], sizeof(float) * s->lda, hA[k], sizeof(float) * s->K, sizeof(float) * s->K,
+                                 s->M_b, cudaMemcpyHostToDevice, s->xfer));
+            CK(cudaEventRecord(s->in_a[q], s->xfer));
+            for (int f = 0; f < s->F; ++f) {
+                const int off = s->offsets[f];
+                CK(cudaMemcpy2DAsync(inB[q] + off, sizeof(float) * s->ldb, hB[k] + off, sizeof(float) * s->N_b,
+                                     sizeof(float) * s->counts[f], s->K, cudaMemcpyHostToDevice, s->xfer));
+                CK(cudaEventRecord(s->in_b[q][f], s->xfer));
+            }
+            return ABFT_OK;
+        };
+        RC(upload(0));
+        bool pending[2] = {false, false};  // a result copy read this C buffer in the previous step
+        for (int k = 0; k < n_steps; ++k) {
+            const int q = k & 1;
+            // the SGEMMs of this step read copy q (sgemm_frag uses s->dA / s->dB)
+            s->dA = inA[q];
+            s->dB = inB[q];
+            int nl = 0, nl2 = 0, nv = 0;
+            CK(cudaStreamWaitEvent(s->verify, s->in_b[q][s->F - 1], 0));
+            RC(launch_encode(s->ws, inA[q], s->lda, inB[q], s->ldb, s->verify, &nl));
+            CK(cudaEventRecord(s->in_free_v[q], s->verify));
+            const cudaEvent_t slot_free[2] = {pending[0] ? s->d2h_done[0] : nullptr,
+                                              pending[1] ? s->d2h_done[1] : nullptr};
+            IoHooks io{s->in_a[q], s->in_b[q].data(), drain ? nullptr : s->c_out.data(), k > 0, slot_free};
+            ak.base_seed = base_seeds[k];
+            RC(enqueue_loop(s, &ak, plans[k], &nl2, &nv, false, &io));
+            CK(cudaEventRecord(s->in_free_c[q], s->compute));
+            // this step's counters, then cleared for the next step
+            CK(cudaMemcpyAsync(&s->ctr_host[k], s->ws->d.ctr, sizeof(Counters), cudaMemcpyDeviceToHost, s->verify));
+            CK(cudaMemsetAsync(s->ws->d.ctr, 0, sizeof(Counters), s->verify));
+            CK(cudaEventRecord(s->vstep, s->verify));
+            res[k] = abft_online_result{};
+            res[k].kernel_launches = nl + nl2;
+            res[k].verify_launches = nv;
+            // the next step's inputs travel while this step computes
+            if (k + 1 < n_steps) RC(upload(k + 1));
+            // this step's result: each fragment once its last check ran (after
+            // the whole step with drain correction)
+            if (drain) CK(cudaStreamWaitEvent(s->xout, s->vstep, 0));
+            const float* last = s->dC[fin];
+            for (int f = 0; f < s->F; ++f) {
+                const int off = s->offsets[f];
+                if (!drain) CK(cudaStreamWaitEvent(s->xout, s->c_out[f], 0));
+                CK(cudaMemcpy2DAsync(hC[k] + off, sizeof(float) * s->N_b, last + off, sizeof(float) * s->ldc,
+                                     sizeof(float) * s->counts[f], s->M_b, cudaMemcpyDeviceToHost, s->xout));
+            }
+            CK(cudaEventRecord(s->d2h_done[fin], s->xout));
+            pending[fin] = true;
+            pending[1 - fin] = false;
+        }
+        CK(cudaEventRecord(s->ojoin, s->xout));
+        CK(cudaEventRecord(s->xjoin, s->xfer));
+        CK(cudaStreamWaitEvent(s->compute, s->vstep, 0));
+        CK(cudaStreamWaitEvent(s->compute, s->ojoin, 0));
+        CK(cudaStreamWaitEvent(s->compute, s->xjoin, 0));
+        CK(cudaEventRecord(s->t1, s->compute));
+        CK(cudaEventSynchronize(s->t1));
+        CK(cudaGetLastError());
+        float ms = 0.f;
+        CK(cudaEventElapsedTime(&ms, s->t0, s->t1));
+        if (e2e_ms) *e2e_ms = ms;
+        int fault = 0;
+        for (int k = 0; k < n_steps; ++k) {
+            const Counters& c = s->ctr_host[k];
+            for (int i = 0; i < 4; ++i) res[k].cm[i] = c.cm[i];
+            res[k].n_restored = c.n_restored;
+            res[k].device_ms = ms / n_steps;
+            res[k].host_ms = 0.0;
+            fault |= c.fault;
+        }
+        if (fault) {
+            set_error("verify: a bulk tensor copy did not complete within the wait limit; the decisions are void");
+            return ABFT_ERR_CUDA;
+        }
+        return ABFT_OK;
+    };
+    const int rc = run();
+    s->dA = origA;
+    s->dB = origB;
+    if (rc != ABFT_OK) {
+        cudaStreamSynchronize(s->xfer);
+        cudaStreamSynchronize(s->xout);
+        cudaStreamSynchronize(s->verify);
+        cudaStreamSynchronize(s->compute);
+    }
+    // the checksums in the workspace belong to the last step's inputs, which
+    // may sit in the second copy: a later online call must encode again
+    s->encoded = false;
     return rc;
 }
 

@@ -157,6 +157,33 @@ class OnlineSession:
         out["e2e_ms"] = e2e.value
         return out
 
+    def run_host_steps(self, hAs, hBs, hCs, base_seeds, mode="none", zone="any", add_delta=ADD_FAULT_DELTA, rank=0,
+                       repeats=1, correct="inloop"):
+        """Several end-to-end steps in one call, step k on (hAs[k], hBs[k]) with
+        base_seeds[k], its final C into hCs[k] (entries may repeat a tensor).
+        Results equal separate run_host calls on the same inputs; the copies of
+        step k+1's inputs overlap step k's work (the session keeps a second
+        device copy of A and B for that). Returns (per-step results, total
+        e2e ms)."""
+        n = len(base_seeds)
+        if not (len(hAs) == len(hBs) == len(hCs) == n) or n < 1:
+            raise ValueError("one hA, hB, hC per step and at least one step")
+        for t in list(hAs) + list(hBs) + list(hCs):
+            if t.is_cuda or t.dtype != torch.float32 or not t.is_contiguous():
+                raise ValueError("host tensors must be contiguous float32 CPU tensors")
+        a = self._args(mode, zone, add_delta, 0, rank, repeats, correct, False)
+        P = ctypes.c_void_p * n
+        pa = P(*[t.data_ptr() for t in hAs])
+        pb = P(*[t.data_ptr() for t in hBs])
+        pc = P(*[t.data_ptr() for t in hCs])
+        seeds = (ctypes.c_uint64 * n)(*[int(x) for x in base_seeds])
+        res = (OnlineResult * n)()
+        e2e = ctypes.c_double()
+        with torch.cuda.device(self.device):
+            call("abft_session_run_host_steps", self.handle, n, pa, pb, pc, ctypes.byref(a), seeds, res,
+                 ctypes.byref(e2e))
+        return [self._result(r) for r in res], e2e.value
+
     def read_log(self, it_count):
         n = it_count * self.F
         ec = np.zeros(n, np.int32)

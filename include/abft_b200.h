@@ -293,6 +293,25 @@ int abft_session_read_injections(abft_session* s, int it_count, int* inj4, float
  * (e2e_ms). hA, hB, hC should be pinned for the copies to be asynchronous. */
 int abft_session_run_host(abft_session* s, const float* hA, const float* hB, float* hC,
                           const abft_online_args* args, abft_online_result* res, double* e2e_ms);
+/* n_steps end-to-end calls back to back, one per input pair: step k copies
+ * hA[k], hB[k] from HOST memory, encodes, runs `repeats` protected iterations
+ * with base_seeds[k] (args->base_seed is ignored) and copies its final C to
+ * hC[k] (entries may alias; copies into one buffer land in step order). Each
+ * step's results are the same as abft_session_run_host's on the same inputs;
+ * res[k] receives step k's counters and launch counts (device_ms = e2e_ms /
+ * n_steps). Unlike n separate calls, the steps overlap: step k+1's inputs
+ * are copied while step k computes, into a second device copy of A and B that
+ * the session allocates on the first call (as large as A and B, freed with
+ * the session; the session's own A and B are overwritten too), and step k's
+ * result is copied back on its own stream while step k+1's SGEMMs run. No
+ * counterpart in the reference, which generates its inputs on the host once
+ * per trial; it is the same loop (pipeline/passes.cuh:90-227) fed from host
+ * memory step after step. Enqueued eagerly (args->graph, log and profile are
+ * ignored); hA, hB, hC should be pinned. e2e_ms: CUDA-event time of all steps,
+ * copies included. */
+int abft_session_run_host_steps(abft_session* s, int n_steps, const float* const* hA, const float* const* hB,
+                                float* const* hC, const abft_online_args* args, const uint64_t* base_seeds,
+                                abft_online_result* res, double* e2e_ms);
 
 /* ------------------------------------------------------------------------
  * Metrics (metrics/metrics.cuh, core/common.cuh:86-106): the confusion

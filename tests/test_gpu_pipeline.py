@@ -208,3 +208,59 @@ def test_tile_seed_scheme(graph, abft, orc):
     compare(s, res, o, 10)
     assert res["cm"][0] == 10 and res["n_restored"] == 10
     s.close()
+
+
+@pytest.mark.parametrize("mode,correct,repeats", [("add", "inloop", 6), ("swifi", "drain", 5), ("swifi", "inloop", 5),
+                                                  ("none", "inloop", 4)])
+def test_run_host_steps(mode, correct, repeats, abft, orc):
+    """Four steps on four different inputs in one run_host_steps call (inputs
+    of step k+1 copied while step k computes, a second device copy of A and B
+    reused from step 2 on): every step's counters and final C equal a
+    separate run_host call on the same inputs and the oracle's replay on that
+    step's own fault-free C, bit for bit."""
+    M, K, N, F = 768, 512, 1024, 4
+    s, A0, B0, counts, offsets, tau, _ = make_session(abft, orc, M, K, N, F, 31, 32)
+    steps = [tiles(orc, M, K, N, 100 + k, 200 + k) for k in range(4)]
+    seeds = [1000 + 31337 * k for k in range(4)]
+    hAs = [torch.from_numpy(A).pin_memory() for A, _ in steps]
+    hBs = [torch.from_numpy(B).pin_memory() for _, B in steps]
+    want = []
+    for k, (A, B) in enumerate(steps):
+        # the oracle replays the step on the GPU's own fault-free C of its inputs
+        s.A.copy_(hAs[k].cuda())
+        s.B.copy_(hBs[k].cuda())
+        torch.cuda.synchronize()  # the session's streams are not ordered after torch's
+        s.baseline(1)
+        torch.cuda.synchronize()
+        clean = s.C[0].cpu().numpy().copy()
+        o = orc.online_loop(clean, A, B, counts, offsets, tau, mode, "any", 1.0e6, seeds[k], 0, repeats)
+        hC = torch.empty((M, N), dtype=torch.float32).pin_memory()
+        r = s.run_host(hAs[k], hBs[k], hC, mode, "any", base_seed=seeds[k], repeats=repeats, correct=correct)
+        assert r["cm"] == list(o["cm"])
+        want.append((r, hC.numpy().copy(), o))
+    hCs = [torch.zeros((M, N), dtype=torch.float32).pin_memory() for _ in range(4)]
+    got, e2e = s.run_host_steps(hAs, hBs, hCs, seeds, mode, "any", repeats=repeats, correct=correct)
+    assert e2e > 0 and len(got) == 4
+    fin = "buf1" if (repeats - 1) & 1 else "buf0"
+    for k in range(4):
+        r, c_single, o = want[k]
+        assert got[k]["cm"] == r["cm"] == list(o["cm"]), k
+        assert got[k]["n_restored"] == r["n_restored"]
+        assert got[k]["verify_launches"] == repeats * F
+        h = hCs[k].numpy()
+        assert np.array_equal(h.view(np.uint32), c_single.view(np.uint32)), k
+        assert np.array_equal(h.view(np.uint32), o[fin].view(np.uint32)), k
+    if mode != "none":
+        assert sum(g["cm"][0] for g in got) > 0
+    # a second call reuses the session's step resources; one host buffer may serve every step
+    one = torch.zeros((M, N), dtype=torch.float32).pin_memory()
+    got2, _ = s.run_host_steps(hAs[:3], hBs[:3], [one] * 3, seeds[:3], mode, "any", repeats=repeats, correct=correct)
+    assert [g["cm"] for g in got2] == [g["cm"] for g in got[:3]]
+    assert np.array_equal(one.numpy().view(np.uint32), hCs[2].numpy().view(np.uint32))
+    # the workspace now holds the last step's checksums: an online call encodes its own inputs again
+    s.A.copy_(hAs[0].cuda())
+    s.B.copy_(hBs[0].cuda())
+    torch.cuda.synchronize()
+    res = s.online("add", base_seed=5, repeats=2)
+    assert res["cm"][0] == 2 and res["cm"][2] == 0
+    s.close()
