@@ -6,6 +6,7 @@
 //   torchrun --nproc-per-node 8 --no-python ./abft_gemm 8192 --grid 2 4 ...
 
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 
 #include <algorithm>
 #include <chrono>
@@ -365,6 +366,15 @@ int main(int argc, char** argv) {
     }
     for (int t = 0; t < (cfg.calibrate ? 0 : TOTAL); ++t) {
         const bool record = (t >= NUM_WARMUP);
+        // profiler range of this trial (warm-up or recorded); a no-op without a tool
+        struct TrialRange {
+            explicit TrialRange(int t, bool rec) {
+                char buf[48];
+                std::snprintf(buf, sizeof(buf), "abft trial %d (%s)", t, rec ? "recorded" : "warm-up");
+                nvtxRangePushA(buf);
+            }
+            ~TrialRange() { nvtxRangePop(); }
+        } trial_range(t, record);
         if (cfg.reseed_per_trial) {
             if (int r = regen(cfg.seed_a + (unsigned long long)t * 1000003ull, cfg.seed_b + (unsigned long long)t * 1000033ull))
                 return r;

@@ -16,9 +16,11 @@
 
 #include <cublas_v2.h>
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 
 #include <algorithm>
 #include <chrono>
+#include <cstdio>
 #include <new>
 #include <string>
 #include <vector>
@@ -85,6 +87,21 @@ struct abft_session {
 };
 
 namespace {
+
+// A named range on the host timeline of a profiler (Nsight Systems, or ncu
+// --nvtx filters); without an attached tool each call returns at once.
+struct NvtxRange {
+    explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+    // printf-style name with one integer field ("abft step %d")
+    NvtxRange(const char* fmt, int v) {
+        char buf[64];
+        std::snprintf(buf, sizeof(buf), fmt, v);
+        nvtxRangePushA(buf);
+    }
+    ~NvtxRange() { nvtxRangePop(); }
+    NvtxRange(const NvtxRange&) = delete;
+    NvtxRange& operator=(const NvtxRange&) = delete;
+};
 
 #define CK(call)                                                     \
     do {                                                             \
@@ -197,6 +214,7 @@ int enqueue_loop(abft_session* s, const abft_online_args* a, const std::vector<P
     bool first[2] = {true, true};
     int nl = 0, nv = 0;
     for (int it = 0; it < a->repeats; ++it) {
+        const NvtxRange range("abft iteration %d", it);
         const int bi = it & 1;
         float* dC = s->dC[bi];
         if (used[bi]) CK(cudaStreamWaitEvent(s->compute, s->buf_done[bi], 0));
@@ -555,6 +573,7 @@ int abft_session_encode(abft_session* s, double* encode_ms) {
         set_error("abft_session_encode: NULL session");
         return ABFT_ERR_ARG;
     }
+    const NvtxRange range("abft encode");
     CK(cudaEventRecord(s->t0, s->verify));
     RC(launch_encode(s->ws, s->dA, s->lda, s->dB, s->ldb, s->verify, nullptr));
     CK(cudaEventRecord(s->t1, s->verify));
@@ -571,6 +590,7 @@ int abft_session_baseline(abft_session* s, int repeats, int graph, double* devic
         set_error("abft_session_baseline: bad argument");
         return ABFT_ERR_ARG;
     }
+    const NvtxRange range(graph ? "abft baseline pass (graph)" : "abft baseline pass");
     CK(cudaStreamSynchronize(s->compute));
     if (graph && (!s->bexec || s->b_repeats != repeats)) {
         if (s->bexec) cudaGraphExecDestroy(s->bexec);
@@ -618,6 +638,7 @@ int abft_session_online(abft_session* s, const abft_online_args* a, abft_online_
         return ABFT_ERR_ARG;
     }
     RC(check_args(s, a));
+    const NvtxRange range(a->graph ? "abft online loop (graph)" : "abft online loop");
     s->profile = a->profile ? 1 : 0;
     if (!s->encoded) {
         double ms;
@@ -700,6 +721,7 @@ int abft_session_run_host(abft_session* s, const float* hA, const float* hB, flo
         return ABFT_ERR_ARG;
     }
     RC(check_args(s, a));
+    const NvtxRange range("abft run_host");
     s->profile = a->profile ? 1 : 0;
     if (a->repeats < 1) {
         set_error("abft_session_run_host: repeats must be >= 1");
@@ -815,6 +837,7 @@ int abft_session_run_host_steps(abft_session* s, int n_steps, const float* const
         return ABFT_ERR_ARG;
     }
     RC(ensure_step_resources(s, n_steps));
+    const NvtxRange range("abft run_host_steps (%d steps)", n_steps);
     s->profile = 0;
     std::vector<std::vector<Plan>> plans(n_steps);
     for (int k = 0; k < n_steps; ++k) {
@@ -860,6 +883,7 @@ int abft_session_run_host_steps(abft_session* s, int n_steps, const float* const
         RC(upload(0));
         bool pending[2] = {false, false};  // a result copy read this C buffer in the previous step
         for (int k = 0; k < n_steps; ++k) {
+            const NvtxRange step_range("abft step %d", k);
             const int q = k & 1;
             // the SGEMMs of this step read copy q (sgemm_frag uses s->dA / s->dB)
             s->dA = inA[q];
