@@ -24,10 +24,32 @@ def free_port():
     return p
 
 
-def torchrun(n, args, timeout=600):
+def free_ports(n):
+    """The first of n free consecutive loopback ports."""
+    for _ in range(50):
+        base = free_port()
+        if base + n >= 65535:
+            continue
+        socks = []
+        try:
+            for p in range(base, base + n):
+                s = socket.socket()
+                socks.append(s)
+                s.bind(("127.0.0.1", p))
+            return base
+        except OSError:
+            continue
+        finally:
+            for s in socks:
+                s.close()
+    raise RuntimeError("no free port range")
+
+
+def torchrun(n, args, timeout=600, env_extra=None):
     cmd = ["timeout", "-k", "30", str(timeout), sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            f"--nproc-per-node={n}", "--master-addr=127.0.0.1", f"--master-port={free_port()}"] + args
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    env.update(env_extra or {})
     return subprocess.run(cmd, capture_output=True, text=True, timeout=timeout + 60, env=env, cwd=ROOT)
 
 
@@ -81,3 +103,38 @@ def test_driver_all_gpus_graph_swifi(tmp_path):
     assert (row["Pr"], row["Pc"]) == GRIDS[n]
     assert int(row["TP"]) + int(row["TN"]) + int(row["FP"]) + int(row["FN"]) == n * 6 * 2 * 4
     assert int(row["FP"]) == 0 and int(row["TP"]) + int(row["FN"]) == n * 6 * 2
+
+
+REF_MPI = os.path.join(ROOT, "oracle", "_ref", "abft_gemm_ref_mpi")
+TIMING_COLS = {"baseline_min_ms", "baseline_median_ms", "baseline_mean_ms", "baseline_max_ms",
+               "baseline_gflops_min", "baseline_gflops_median", "baseline_gflops_mean", "baseline_gflops_max",
+               "protected_min_ms", "protected_median_ms", "protected_mean_ms", "protected_max_ms",
+               "protected_gflops_min", "protected_gflops_median", "protected_gflops_mean", "protected_gflops_max",
+               "overhead_pct"}
+
+
+@pytest.mark.skipif(not os.path.exists(REF_MPI), reason="multi-rank reference driver not built")
+@pytest.mark.parametrize("grid", [["1", "2"], ["2", "1"]])
+def test_reference_binary_two_ranks(grid, tmp_path):
+    """The reference driver itself as two ranks (its MPI calls carried by the
+    loopback stand-in, one GPU per rank) against abft_gemm with the same grid,
+    flags and seeds: every non-timing CSV column (confusion matrix, restore
+    count, threshold, geometry) must be equal."""
+    args = ["2048", "1024", "2048", "--grid", *grid, "--inject", "swifi", "--threshold", "0.02", "--repeats", "6",
+            "--samples", "2", "--warmups", "1"]
+    ref_csv, ours_csv = str(tmp_path / "ref.csv"), str(tmp_path / "ours.csv")
+    # the reference picks its GPU from OMPI_COMM_WORLD_LOCAL_RANK (main.cu:43-47)
+    wrap = 'OMPI_COMM_WORLD_LOCAL_RANK=$LOCAL_RANK exec "$0" "$@"'
+    r = torchrun(2, ["--no-python", "bash", "-c", wrap, REF_MPI] + args + ["--csv", ref_csv],
+                 env_extra={"ABFT_MPI_STUB_PORT": str(free_ports(2)), "ABFT_MPI_STUB_TIMEOUT": "120"})
+    assert r.returncode == 0, (r.stdout[-2000:], r.stderr[-3000:])
+    drv = os.path.join(ROOT, PKG_NAME, "abft_gemm")
+    r = torchrun(2, ["--no-python", drv] + args + ["--csv", ours_csv])
+    assert r.returncode == 0, (r.stdout[-2000:], r.stderr[-3000:])
+    ref = list(csv.DictReader(open(ref_csv)))[0]
+    ours = list(csv.DictReader(open(ours_csv)))[0]
+    assert list(ours.keys()) == list(ref.keys())
+    for k in ref:
+        if k not in TIMING_COLS:
+            assert ours[k] == ref[k], (k, ours[k], ref[k])
+    assert (ref["Pr"], ref["Pc"]) == tuple(grid) and int(ref["TP"]) + int(ref["FN"]) == 2 * 6 * 2
