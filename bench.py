@@ -11,6 +11,7 @@ broadcast from rank 0 over NCCL before timing.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--verify-kernel auto|ldg|tma] [--timeline TRACE_JSON]
+    python bench.py --verify-sweep [--verify-kernel auto|ldg|tma]
 
 Rank 0 prints one JSON line. `value` is whole-job protected TFLOP/s
 (2*M*N*K*iterations / max-over-ranks device time); `e2e` the same through
@@ -56,6 +57,9 @@ def parse():
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--verify-kernel", choices=["auto", "ldg", "tma"], default="auto",
                    help="verify body: by fragment size, 128-bit loads, or TMA-staged")
+    p.add_argument("--verify-sweep", action="store_true",
+                   help="instead of the benchmark: the verify kernel alone on the fragment shapes of the "
+                        "workloads (L2 emptied before each launch, mean of 30 launches), one JSON line per shape")
     p.add_argument("--timeline", default=None, metavar="TRACE_JSON",
                    help="after the timed runs, record one protected trial with the CUDA profiler (CUPTI "
                         "kernel records, cuBLAS included) into this Chrome trace and report how much of "
@@ -536,8 +540,54 @@ def run_ours(args):
     dist_mod.shutdown()
 
 
+# Fragment shapes (rows M_b, columns N_f, row pitch) of the workloads: F = 4
+# fragments of the rank tile, from 1024^3 to 16384^3 on one GPU, the 2x4
+# grid's tiles, the non-square shapes, and a 1 GiB fragment.
+SWEEP_SHAPES = [(1024, 256, 1024), (4096, 512, 2048), (4096, 1024, 4096), (16384, 256, 1024),
+                (1024, 4096, 16384), (8192, 1024, 4096), (8192, 2048, 8192), (16384, 2048, 8192),
+                (16384, 4096, 16384), (65536, 4096, 4096)]
+
+
+def verify_sweep(args):
+    """The verify kernel alone per fragment shape (body selected by
+    --verify-kernel): L2 emptied before each launch, CUDA events on the
+    launching stream, mean of 30 launches after 3 untimed ones."""
+    import torch
+    abft = importlib.import_module(PKG)
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    abft.set_verify_kernel(args.verify_kernel)
+    peak, peak_kind = peak_hbm()
+    cold = ColdL2(torch, dev)
+    st = torch.cuda.Stream(device=dev)
+    for M, N, ldc in SWEEP_SHAPES:
+        C = torch.randn((M, ldc), dtype=torch.float32, device=dev)
+        ws = abft.kernels.Workspace(M, ldc, 64, [N], [0])
+        times = []
+        with torch.cuda.stream(st):
+            for k in range(33):
+                cold()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(st)
+                abft.host.call("abft_verify", ws.handle, C.data_ptr(), ldc, 0, 1e30, 0, -1, st.cuda_stream)
+                e1.record(st)
+                e1.synchronize()
+                if k >= 3:
+                    times.append(e0.elapsed_time(e1) * 1e3)
+        ws.close()
+        del C
+        us = statistics.mean(times)
+        nbytes = 4.0 * M * N + 24.0 * N
+        print(json.dumps({"fragment": [M, N], "ldc": ldc, "bytes": nbytes, "verify_kernel": args.verify_kernel,
+                          "mean_us": us, "median_us": statistics.median(times), "achieved_gbs": nbytes / us / 1e3,
+                          "frac": nbytes / us / 1e3 / peak, "peak_gbs": peak, "peak_kind": peak_kind}), flush=True)
+
+
 def main():
     args = parse()
+    if args.verify_sweep:
+        verify_sweep(args)
+        return
     if args.warmup < 3:
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
     if args.impl == "reference":
