@@ -1,5 +1,6 @@
 """Multi-rank plumbing on CPU (gloo): panel distribution over the Pr x Pc grid
-and the metric reductions, with world sizes 2, 4 and 8 (grids 1x2, 2x2, 2x4)."""
+and the metric reductions, with world sizes 2, 3, 4, 6 and 8 (grids 1x2, 1x3,
+2x2, 2x3, 2x4), tiles ragged where the sizes do not divide."""
 import os
 import socket
 
@@ -48,7 +49,8 @@ def worker(rank, world, port, M, K, N, q):
         q.put((rank, False, repr(e), None, None))
 
 
-@pytest.mark.parametrize("world,shape", [(2, (300, 40, 517)), (4, (301, 33, 250)), (8, (257, 17, 130))])
+@pytest.mark.parametrize("world,shape", [(2, (300, 40, 517)), (3, (97, 21, 302)), (4, (301, 33, 250)),
+                                         (6, (301, 29, 1000)), (8, (257, 17, 130))])
 def test_panels_and_reductions(world, shape):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
