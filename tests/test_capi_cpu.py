@@ -156,3 +156,35 @@ def test_session_arguments_are_validated(abft):
     # an unknown SWIFI zone means the whole word, as in the reference (kernels/swifi.cuh:25-31)
     z = OnlineSession._args(None, "swifi", "mantissa", 1.0, 0, 0, 1, "inloop", False)
     assert (z.zone_lo, z.zone_hi) == (0, 31)
+
+
+C_CLIENT = r"""
+#include "abft_b200.h"
+#include <stdio.h>
+int main(void) {
+    int counts[4], offsets[4], Pr = 0, Pc = 0;
+    if (abft_split_dim(1030, 4, counts, offsets) != ABFT_OK) return 1;
+    if (abft_choose_grid(8, &Pr, &Pc) != ABFT_OK || Pr * Pc != 8) return 2;
+    if (abft_verify(NULL, NULL, 0, 0, 1.0, 0, -1, NULL) != ABFT_ERR_ARG) return 3;
+    printf("%d %d %d %d %dx%d\n", counts[0], counts[1], counts[2], counts[3], Pr, Pc);
+    return 0;
+}
+"""
+
+
+def test_header_is_a_plain_c_abi(abft, tmp_path):
+    """include/abft_b200.h compiles as strict C99 and a C program links and
+    calls libabft_b200.so (what a cgo / JNI / ctypes binding needs)."""
+    import os
+    import subprocess
+    src = tmp_path / "client.c"
+    src.write_text(C_CLIENT)
+    exe = str(tmp_path / "client")
+    libdir = os.path.dirname(abft.LIB_PATH)
+    r = subprocess.run(["gcc", "-std=c99", "-Wall", "-Wextra", "-pedantic", "-Werror", "-I",
+                        os.path.dirname(abft.HEADER_PATH), "-o", exe, str(src), "-L", libdir, "-labft_b200",
+                        f"-Wl,-rpath,{libdir}"], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0, (r.returncode, r.stderr)
+    assert r.stdout.split() == ["258", "258", "257", "257", "2x4"]
