@@ -52,3 +52,25 @@ def test_help_lists_reference_flags_and_extensions():
                  "--relative-threshold", "--correct", "--verify-priority", "--csv-extra", "--graph",
                  "--inject-seed-mode"):
         assert flag in r.stdout, flag
+
+
+def test_sweep_commands_are_valid_driver_invocations(tmp_path):
+    """The throughput sweep (the reference's example_run.sh protocol: per size
+    --baseline, --inject none, --inject add) builds driver command lines that
+    the driver accepts: on a machine without a GPU each stops at the first CUDA
+    call (exit 1), never at argument parsing (exit 2)."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("abft_sweep", os.path.join(ROOT, PKG_NAME, "sweep.py"))
+    sweep = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(sweep)
+    k = sweep.knobs({"SIZES": "64 96", "F": "4", "SAMPLES": "1", "WARMUPS": "0",
+                     "OUT_CSV": str(tmp_path / "m.csv")})
+    runs = sweep.commands(k, ["--graph"])
+    assert [label for label, _ in runs] == [f"S = {s}, {m}" for s in (64, 96) for m, _ in sweep.MODES]
+    for label, argv in runs:
+        assert argv[0] == DRIVER and "--graph" in argv and "--csv" in argv
+        r = run(*argv[1:], cwd=str(tmp_path))
+        assert r.returncode in (0, 1), (label, r.returncode, r.stderr)
+        assert "flag" not in r.stderr and "must be" not in r.stderr, (label, r.stderr)
+    multi = sweep.commands(dict(k, NP=8))
+    assert all("--nproc-per-node=8" in argv and DRIVER in argv for _, argv in multi)
