@@ -121,6 +121,7 @@ SIGNATURES = {
     "abft_calibrate": (_I, [_P, _P, _I64, _I, _P, _P]),
     "abft_verify_noalloc": (_I, [_P, _I64, _I, _I, _P, _D, _I, _P, _P, _P, _P]),
     "abft_set_verify_kernel": (_I, [_I]),
+    "abft_set_wait_limit": (_I, [_I]),
     "abft_localize_correct": (_I, [_P, _P, _I64, _I, _D, _I, _P, _I64, _I, _I, _P]),
     "abft_drain": (_I, [_P, _P, _P, _I64, _P, _I64, _I, _P]),
     "abft_inject_add": (_I, [_P, _I64, _I, _I, _F, _P]),

@@ -48,7 +48,7 @@ WsLayout ws_layout(int M_b, int N_b, int K, int F, int nfmax, int max_iters) {
     L.vact = take(sizeof(double) * nfpad);
     L.vd = take(sizeof(double) * nfpad);
     L.vw = take(sizeof(double) * nfpad);
-    L.vcnt = take(sizeof(int) * (groups + 1));
+    L.vcnt = take(sizeof(int) * (kArriveGroup + groups));
     L.lact = take(sizeof(double) * M_b);
     L.ld = take(sizeof(double) * M_b);
     L.lw = take(sizeof(double) * M_b);
@@ -296,6 +296,15 @@ int abft_set_verify_kernel(int which) {
     const int prev = set_verify_kernel(which);
     if (prev < 0) {
         set_error("abft_set_verify_kernel: which must be ABFT_VERIFY_AUTO, _LDG or _TMA");
+        return ABFT_ERR_ARG;
+    }
+    return prev;
+}
+
+int abft_set_wait_limit(int polls) {
+    const int prev = set_wait_limit(polls);
+    if (prev < 0) {
+        set_error("abft_set_wait_limit: polls must be >= 0");
         return ABFT_ERR_ARG;
     }
     return prev;

@@ -14,6 +14,13 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kGroupCols = 128;  // columns per verify CTA: 32 lanes x 4 columns
 constexpr int kMaxChunks = 1024; // row chunks per column group (verify grid.y)
 constexpr int kVerifySmemMax = 64 * 1024;  // verify dynamic shared memory cap
+// Arrival state of one verify launch, in WsDev::vcnt (all zero between launches):
+//   [kArriveFinal]      column groups that have finished (the last one decides the fragment)
+//   [kArriveCand]       set when some group holds a column whose |actual - expected| may exceed tau
+//   [kArriveGroup + g]  CTAs of column group g that have finished (the last one finishes the group)
+constexpr int kArriveFinal = 0;
+constexpr int kArriveCand = 1;
+constexpr int kArriveGroup = 2;
 
 // Per-fragment decision record (the reference's dErrCol[f] / dRowDiff[f],
 // plus the located row).
@@ -71,7 +78,7 @@ struct WsDev {
     double* vact;      // [nfpad]
     double* vd;
     double* vw;
-    int* vcnt;         // [groups_max + 1]
+    int* vcnt;         // [kArriveGroup + groups_max]
     double* lact;      // [M_b]
     double* ld;
     double* lw;
@@ -127,6 +134,9 @@ int launch_inject(float* dC, int64_t ldc, int row, int col, int mode, float delt
 int set_verify_kernel(int which);
 // The current selection (ABFT_VERIFY_*).
 int verify_kernel();
+// Polls each wait of the TMA verify body makes before it gives up; returns the
+// previous limit, or -1 for a negative one.
+int set_wait_limit(int polls);
 int launch_verify_static(const float* Cf, int64_t ldc, int M, int N, const double* expv, double tau, int injected,
                          int* errcol, double* rowdiff, int* cm, cudaStream_t st);
 

@@ -102,9 +102,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Bounded wait for the phase with the given parity to complete.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-    for (int i = 0; i < kSpinLimit; ++i)
+// Bounded wait for the phase with the given parity to complete (at most
+// `limit` polls).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int limit = kSpinLimit) {
+    for (int i = 0; i < limit; ++i)
         if (mbar_try_wait(bar, parity)) return true;
     return false;
 }
@@ -408,32 +409,36 @@ __device__ int final_select(int n, double tau, const double* __restrict__ expv, 
 
 // ------------------------------------------------------------- verify -----
 
-// Second half of the verify kernels: fold the CTA's per-column partials
-// (S, |x|-sum, smallest |x| bits - 1 of columns c0..c0+3 in each thread) into
-// the per-column accumulators; the last CTA to arrive certifies every column
-// and runs the reference's arg-max (or writes the calibration differences).
-// dsm: at least kWarps * kGroupCols * 16 bytes of dynamic shared memory that
-// no copy writes any more.
-__device__ __forceinline__ void verify_tail(unsigned char* dsm, SelectSmem& sel, double s0, double s1, double s2,
-                                            double s3, float t0, float t1, float t2, float t3, uint32_t m0,
-                                            uint32_t m1, uint32_t m2, uint32_t m3, const float* __restrict__ C,
-                                            long long ldc, int M, int N, int total_ctas, int dw_in_smem,
+// Second half of the verify kernels. Every CTA of column group g = blockIdx.x
+// folds its per-column partials (S, |x|-sum, smallest |x| bits - 1 of columns
+// c0..c0+3 in each thread) into the group's accumulators (skipped with fold =
+// false: a CTA whose copies did not all land adds nothing, and its launch is
+// void). The last of the group's gridDim.y CTAs certifies the group's 128
+// columns (in parallel with the other groups' streaming) and votes whether any
+// may exceed tau; the last group to finish runs the reference's arg-max only
+// when some group voted yes (or, calibrating, each group writes its own
+// columns' exact differences). Shared memory touched: dsm (kWarps * kGroupCols
+// * 16 bytes, for the fold only) and sel.
+__device__ __forceinline__ void verify_tail(unsigned char* dsm, SelectSmem& sel, bool fold, double s0, double s1,
+                                            double s2, double s3, float t0, float t1, float t2, float t3,
+                                            uint32_t m0, uint32_t m1, uint32_t m2, uint32_t m3,
+                                            const float* __restrict__ C, long long ldc, int M, int N,
                                             const double* __restrict__ expv, double tau, int injected, int f, int F,
                                             int it, const WsDev& w, double* calib_out,
                                             cudaGraphConditionalHandle cond) {
-    double(*s_s)[kGroupCols] = reinterpret_cast<double(*)[kGroupCols]>(dsm);
-    float(*s_t)[kGroupCols] = reinterpret_cast<float(*)[kGroupCols]>(dsm + kWarps * kGroupCols * 8);
-    uint32_t(*s_m)[kGroupCols] = reinterpret_cast<uint32_t(*)[kGroupCols]>(dsm + kWarps * kGroupCols * 12);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = blockIdx.x;
-    const int cl = lane * 4;
-    s_s[warp][cl + 0] = s0; s_s[warp][cl + 1] = s1; s_s[warp][cl + 2] = s2; s_s[warp][cl + 3] = s3;
-    s_t[warp][cl + 0] = t0; s_t[warp][cl + 1] = t1; s_t[warp][cl + 2] = t2; s_t[warp][cl + 3] = t3;
-    s_m[warp][cl + 0] = m0; s_m[warp][cl + 1] = m1; s_m[warp][cl + 2] = m2; s_m[warp][cl + 3] = m3;
-    __syncthreads();
-    if (tid < kGroupCols) {
-        const int col = g * kGroupCols + tid;
-        if (col < N) {
+    const int col = g * kGroupCols + tid;  // the column this thread finishes (tid < kGroupCols)
+    if (fold) {
+        double(*s_s)[kGroupCols] = reinterpret_cast<double(*)[kGroupCols]>(dsm);
+        float(*s_t)[kGroupCols] = reinterpret_cast<float(*)[kGroupCols]>(dsm + kWarps * kGroupCols * 8);
+        uint32_t(*s_m)[kGroupCols] = reinterpret_cast<uint32_t(*)[kGroupCols]>(dsm + kWarps * kGroupCols * 12);
+        const int cl = lane * 4;
+        s_s[warp][cl + 0] = s0; s_s[warp][cl + 1] = s1; s_s[warp][cl + 2] = s2; s_s[warp][cl + 3] = s3;
+        s_t[warp][cl + 0] = t0; s_t[warp][cl + 1] = t1; s_t[warp][cl + 2] = t2; s_t[warp][cl + 3] = t3;
+        s_m[warp][cl + 0] = m0; s_m[warp][cl + 1] = m1; s_m[warp][cl + 2] = m2; s_m[warp][cl + 3] = m3;
+        __syncthreads();
+        if (tid < kGroupCols && col < N) {
             double S = 0.0;
             float T = 0.f;
             uint32_t mb = kFull;
@@ -450,66 +455,78 @@ __device__ __forceinline__ void verify_tail(unsigned char* dsm, SelectSmem& sel,
     }
     fence_acq_rel_gpu();
     __syncthreads();
-    if (tid == 0) sel.flag = (atomicAdd(w.vcnt, 1) == total_ctas - 1);
+    if (tid == 0) sel.flag = (atomicAdd(w.vcnt + kArriveGroup + g, 1) == (int)gridDim.y - 1);
     __syncthreads();
     if (!sel.flag) return;
     fence_acq_rel_gpu();
 
-    // Last CTA: certify every column, reset the accumulators for the next launch.
-    // Loads of a batch are issued before any store so that they overlap.
-    double* dd = dw_in_smem ? reinterpret_cast<double*>(dsm) : w.vd;
-    double* ww = dw_in_smem ? reinterpret_cast<double*>(dsm) + N : w.vw;
-    for (int base = 0; base < N; base += 4 * kThreads) {
-        double S[4], E[4];
-        float T[4];
-        uint32_t MB[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int j = base + u * kThreads + tid;
-            if (j < N) {
-                S[u] = __ldcg(w.vacc_s + j);
-                T[u] = __ldcg(w.vacc_t + j);
-                MB[u] = __ldcg(w.vacc_m + j);
-                E[u] = expv[j];
-            }
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int j = base + u * kThreads + tid;
-            if (j < N) {
-                w.vacc_s[j] = 0.0;
-                w.vacc_t[j] = 0.f;
-                w.vacc_m[j] = kFull;
-                const double d = fabs(S[u] - E[u]);
-                w.vact[j] = S[u];
-                dd[j] = d;
-                ww[j] = cert_window(S[u], T[u], MB[u], M, d);
-            }
-        }
+    // Last CTA of the group: certify its columns, reset their accumulators.
+    double d = 0.0, wv = 0.0;
+    int cand = 0;
+    if (tid < kGroupCols && col < N) {
+        const double S = __ldcg(w.vacc_s + col);
+        const float T = __ldcg(w.vacc_t + col);
+        const uint32_t mb = __ldcg(w.vacc_m + col);
+        const double E = expv[col];
+        w.vacc_s[col] = 0.0;
+        w.vacc_t[col] = 0.f;
+        w.vacc_m[col] = kFull;
+        d = fabs(S - E);
+        wv = cert_window(S, T, mb, M, d);
+        w.vact[col] = S;
+        w.vd[col] = d;
+        w.vw[col] = wv;
+        cand = (d + wv > tau) ? 1 : 0;
     }
-    __syncthreads();
-
     if (calib_out != nullptr) {
         // Calibration (pass_calibrate, pipeline/passes.cuh:66-84): every
-        // |actualRow - expectedRow| exactly, uncertified columns re-summed in
-        // the reference's order; no detection, no counters.
-        for (int j = warp; j < N; j += kWarps) {
-            if (ww[j] != 0.0) {
+        // |actualRow - expectedRow| exactly, the group's uncertified columns
+        // re-summed in the reference's order (one warp per column); no
+        // detection, no counters.
+        if (tid < kGroupCols) sel.d[tid] = (col < N) ? wv : 0.0;
+        __syncthreads();
+        for (int c = warp; c < kGroupCols; c += kWarps) {
+            const int j = g * kGroupCols + c;
+            if (j < N && sel.d[c] != 0.0) {
                 const double S = exact_chain(C + j, ldc, M);
-                if (lane == 0) dd[j] = fabs(S - expv[j]);
+                if (lane == 0) calib_out[j] = fabs(S - expv[j]);
             }
         }
-        __syncthreads();
-        for (int j = tid; j < N; j += kThreads) calib_out[j] = dd[j];
-        if (tid == 0) *w.vcnt = 0;
+        if (tid < kGroupCols && col < N && wv == 0.0) calib_out[col] = d;
+        cand = 0;
+    }
+    fence_acq_rel_gpu();
+    cand = __syncthreads_or(cand);
+    if (tid == 0) {
+        w.vcnt[kArriveGroup + g] = 0;  // every CTA of the group has arrived
+        if (cand) atomicOr(w.vcnt + kArriveCand, 1);
+        fence_acq_rel_gpu();
+        sel.flag = (atomicAdd(w.vcnt + kArriveFinal, 1) == (int)gridDim.x - 1);
+    }
+    __syncthreads();
+    if (!sel.flag) return;
+    fence_acq_rel_gpu();
+
+    // Last group: the fragment's decision.
+    if (tid == 0) sel.cnt = __ldcg(w.vcnt + kArriveCand);
+    __syncthreads();
+    const int any = sel.cnt;
+    __syncthreads();
+    if (calib_out != nullptr) {
+        if (tid == 0) {
+            w.vcnt[kArriveFinal] = 0;
+            w.vcnt[kArriveCand] = 0;
+        }
         return;
     }
-
-    // The reference's detection (k_detect_row) on exact values.
-    const int ec = final_select<false>(
-        N, tau, expv, w.vact, dd, ww, [&](int j) { return exact_chain(C + j, ldc, M); }, sel);
+    // The reference's detection (k_detect_row) on exact values; a fragment in
+    // which no column can exceed tau has no winner.
+    int ec = -1;
+    if (any)
+        ec = final_select<true>(N, tau, expv, w.vact, w.vd, w.vw,
+                                [&](int j) { return exact_chain(C + j, ldc, M); }, sel);
     if (tid == 0) {
-        const double rd = (ec >= 0) ? (w.vact[ec] - expv[ec]) : 0.0;
+        const double rd = (ec >= 0) ? (__ldcg(w.vact + ec) - expv[ec]) : 0.0;
         w.rec[f].errcol = ec;
         w.rec[f].errrow = -1;
         w.rec[f].rowdiff = rd;
@@ -525,7 +542,8 @@ __device__ __forceinline__ void verify_tail(unsigned char* dsm, SelectSmem& sel,
             L.errrow = -1;
             L.rowdiff = rd;
         }
-        *w.vcnt = 0;
+        w.vcnt[kArriveFinal] = 0;
+        w.vcnt[kArriveCand] = 0;
     }
 }
 
@@ -540,8 +558,7 @@ __device__ __forceinline__ void verify_tail(unsigned char* dsm, SelectSmem& sel,
 // reused by the last CTA for the d / w arrays when 16*N bytes fit.
 template <bool VEC>
 __global__ void __launch_bounds__(kThreads, 4)
-    k_verify(const float* __restrict__ C, long long ldc, int M, int N, int rows_per, int total_ctas, int dw_in_smem,
-             const double* __restrict__ expv, double tau, int injected, int f, int F, int it, WsDev w,
+    k_verify(const float* __restrict__ C, long long ldc, int M, int N, int rows_per, const double* __restrict__ expv, double tau, int injected, int f, int F, int it, WsDev w,
              float* Cw, const InjectPlan* __restrict__ plan, int plan_it, float add_delta, int log_inj,
              double* calib_out, cudaGraphConditionalHandle cond) {
     extern __shared__ __align__(16) unsigned char dsm[];
@@ -635,8 +652,8 @@ __global__ void __launch_bounds__(kThreads, 4)
         for (int u = 0; u < kBatch; ++u) acc(v[u]);
     }
 
-    verify_tail(dsm, sel, s0, s1, s2, s3, t0, t1, t2, t3, m0, m1, m2, m3, C, ldc, M, N, total_ctas, dw_in_smem, expv,
-                tau, injected, f, F, it, w, calib_out, cond);
+    verify_tail(dsm, sel, true, s0, s1, s2, s3, t0, t1, t2, t3, m0, m1, m2, m3, C, ldc, M, N, expv, tau, injected, f,
+                F, it, w, calib_out, cond);
 }
 
 // The same fused verify with the tile staged by the Tensor Memory Accelerator:
@@ -649,9 +666,9 @@ __global__ void __launch_bounds__(kThreads, 4)
 // chunk. Requires a 16-byte aligned fragment and ldc % 4 == 0 (tensor map).
 __global__ void __launch_bounds__(kThreads, 2)
     k_verify_tma(const __grid_constant__ CUtensorMap tmap, const float* __restrict__ C, long long ldc, int M, int N,
-                 int rows_per, int total_ctas, int dw_in_smem, const double* __restrict__ expv, double tau,
-                 int injected, int f, int F, int it, WsDev w, float* Cw, const InjectPlan* __restrict__ plan,
-                 int plan_it, float add_delta, int log_inj, double* calib_out, cudaGraphConditionalHandle cond) {
+                 int rows_per, const double* __restrict__ expv, double tau, int injected, int f, int F, int it,
+                 WsDev w, float* Cw, const InjectPlan* __restrict__ plan, int plan_it, float add_delta, int log_inj,
+                 double* calib_out, cudaGraphConditionalHandle cond, int wait_limit) {
     // The dynamic shared memory is launched kTmaAlign bytes larger than the
     // ring and the ring starts at the first kTmaAlign boundary in it: where
     // the dynamic area begins depends on the static shared memory before it
@@ -708,7 +725,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     int fault = 0, k = 0;
     for (; k < nst; ++k) {
         const int st = k % kTmaStages;
-        const bool got = mbar_wait(&full[st], (uint32_t)(k / kTmaStages) & 1u);
+        const bool got = mbar_wait(&full[st], (uint32_t)(k / kTmaStages) & 1u, wait_limit);
         if (got) {
             const float* tile = reinterpret_cast<const float*>(ring + st * kStageBytes);
             const int rb = r0 + k * kTmaRows;
@@ -766,8 +783,10 @@ __global__ void __launch_bounds__(kThreads, 2)
         __syncthreads();
     }
 
-    verify_tail(ring, sel, s0, s1, s2, s3, t0, t1, t2, t3, m0, m1, m2, m3, C, ldc, M, N, total_ctas, dw_in_smem, expv,
-                tau, injected, f, F, it, w, calib_out, cond);
+    // After a fault the ring may still receive a late copy: the tail then
+    // leaves shared memory other than `sel` alone and adds nothing.
+    verify_tail(ring, sel, !fault, s0, s1, s2, s3, t0, t1, t2, t3, m0, m1, m2, m3, C, ldc, M, N, expv, tau, injected,
+                f, F, it, w, calib_out, cond);
 }
 
 // ----------------------------------------------------------- localise -----
@@ -1171,6 +1190,9 @@ bool fragment_tensor_map(CUtensorMap* map, const float* Cf, int64_t ldc, int M, 
 
 // Which verify body launch_verify uses: 0 = by size, 1 = 128-bit loads, 2 = TMA.
 std::atomic<int> g_verify_kernel{0};
+// Polls each wait of the TMA verify body makes for a bulk copy before it gives
+// up (records a fault); lowered only by tests of that failure path.
+std::atomic<int> g_wait_limit{kSpinLimit};
 
 // Resident CTAs per SM of a kernel at a dynamic shared memory size (cached).
 int resident_per_sm(const void* fn, int smem) {
@@ -1280,31 +1302,24 @@ int launch_verify(abft_ws* ws, const float* dC, int64_t ldc, int f, double tau, 
     if (tma_ok && want_tma && fragment_tensor_map(&map, Cf, ldc, M, N)) {
         const int per_sm = resident_per_sm((const void*)k_verify_tma, kTmaSmem + kTmaAlign);
         verify_geometry_tma(per_sm * ws->sms, M, N, groups, chunks, rows_per);
-        const int dw_in_smem = (16LL * N <= kTmaSmem) ? 1 : 0;
         k_verify_tma<<<dim3(groups, chunks), kThreads, kTmaSmem + kTmaAlign, st>>>(
-            map, Cf, ldc, M, N, rows_per, groups * chunks, dw_in_smem, expv, tau, injected, f, ws->F, it, ws->d, Cw,
-            plan, plan_it, add_delta, log_inj, calib_out, cond);
+            map, Cf, ldc, M, N, rows_per, expv, tau, injected, f, ws->F, it, ws->d, Cw, plan, plan_it, add_delta,
+            log_inj, calib_out, cond, g_wait_limit.load(std::memory_order_relaxed));
         return check_launch("verify (tma)");
     }
 
     const bool vec = aligned16(Cf) && (ldc % 4 == 0) && (N % 4 == 0);
-    // d / w of the last CTA live in the 16 KB reduction area when they fit,
-    // otherwise in the workspace: every CTA keeps a small shared footprint.
-    const int reduce_bytes = kWarps * kGroupCols * 16;
-    const int dw_in_smem = (16LL * N <= reduce_bytes) ? 1 : 0;
-    const int smem = reduce_bytes;
+    // 16 KB of shared memory per CTA: the fold of its eight warps' partials
+    const int smem = kWarps * kGroupCols * 16;
     const int per_sm = resident_per_sm(vec ? (const void*)k_verify<true> : (const void*)k_verify<false>, smem);
     verify_geometry(per_sm * ws->sms, M, N, groups, chunks, rows_per);
     dim3 grid(groups, chunks);
-    const int total = groups * chunks;
     if (vec)
-        k_verify<true><<<grid, kThreads, smem, st>>>(Cf, ldc, M, N, rows_per, total, dw_in_smem, expv, tau,
-                                                     injected, f, ws->F, it, ws->d, Cw, plan, plan_it, add_delta,
-                                                     log_inj, calib_out, cond);
+        k_verify<true><<<grid, kThreads, smem, st>>>(Cf, ldc, M, N, rows_per, expv, tau, injected, f, ws->F, it,
+                                                     ws->d, Cw, plan, plan_it, add_delta, log_inj, calib_out, cond);
     else
-        k_verify<false><<<grid, kThreads, smem, st>>>(Cf, ldc, M, N, rows_per, total, dw_in_smem, expv, tau,
-                                                      injected, f, ws->F, it, ws->d, Cw, plan, plan_it, add_delta,
-                                                      log_inj, calib_out, cond);
+        k_verify<false><<<grid, kThreads, smem, st>>>(Cf, ldc, M, N, rows_per, expv, tau, injected, f, ws->F, it,
+                                                      ws->d, Cw, plan, plan_it, add_delta, log_inj, calib_out, cond);
     return check_launch("verify");
 }
 
@@ -1363,55 +1378,88 @@ int launch_inject(float* dC, int64_t ldc, int row, int col, int mode, float delt
 // in a static device array of this library instead of a workspace, for callers
 // that may not allocate device memory (see include/abft_b200.h). The array is
 // at most kStaticMaxCols columns wide:
-//   [0, 32 KiB)        per-column double sums         (double[4096])
-//   [32 KiB, 48 KiB)   per-column float |x| sums      (float[4096])
-//   [48 KiB, 64 KiB)   per-column smallest |x| bits-1 (uint32[4096], starts at 0xffffffff)
-//   [64 KiB, 96 KiB)   per-column final sums          (double[4096])
-//   then one arrival counter, one decision record and one counter block,
-//   256 bytes each.
-// Every call on a device shares the array. The kernel's last CTA puts the
-// accumulators and the arrival counter back to their start values, and the
-// copy-out kernel zeroes the counter block, so each call starts clean; two
-// calls whose kernels overlap on the GPU race on the array.
+//   [0, 32 KiB)         per-column double sums         (double[4096])
+//   [32 KiB, 48 KiB)    per-column float |x| sums      (float[4096])
+//   [48 KiB, 64 KiB)    per-column smallest |x| bits-1 (uint32[4096], starts at 0xffffffff)
+//   [64 KiB, 96 KiB)    per-column final sums          (double[4096])
+//   [96 KiB, 128 KiB)   per-column |actual - expected| (double[4096])
+//   [128 KiB, 160 KiB)  per-column windows             (double[4096])
+//   then the arrival counters (2 + 32 ints), one decision record and one
+//   counter block, 256 bytes each.
+// Every call in a CUDA context shares that context's copy of the array. The
+// kernel's last CTAs put the accumulators and the arrival counters back to
+// their start values, and the copy-out kernel zeroes the counter block, so
+// each call starts clean; two calls whose kernels overlap on the GPU race on
+// the array.
 namespace abft {
 namespace {
 
 constexpr int kStaticMaxCols = 4096;
-constexpr size_t kStaticColBytes = 96 * 1024;
+constexpr size_t kStaticColBytes = 160 * 1024;
 constexpr size_t kStaticScratchBytes = kStaticColBytes + 3 * 256;
+static_assert(sizeof(int) * (kArriveGroup + kStaticMaxCols / kGroupCols) <= 256, "arrival counters");
 static __device__ __align__(256) unsigned char g_verify_scratch[kStaticScratchBytes];
 
 struct StaticScratchState {
-    bool ready = false;
-    unsigned char* base = nullptr;  // device address of g_verify_scratch on this device
+    unsigned char* base = nullptr;  // device address of g_verify_scratch in this context
     int sms = 0;
 };
-constexpr int kMaxDevices = 64;
 std::mutex g_static_mu;
-StaticScratchState g_static[kMaxDevices];
+// Set-up state per CUDA context: a module's static device array exists once
+// per context, at an address of that context (a second context on a device,
+// or the context that follows cudaDeviceReset, has its own, uncleared copy).
+// Keyed by the driver's context id, which is never reused within a process;
+// where the driver does not offer it, by device and array address.
+std::map<std::pair<unsigned long long, uintptr_t>, StaticScratchState> g_static;
 
-// One-time set-up per device, with that device current: resolve the device
-// address of the static array (host code may not use the symbol itself) and
-// bring it to its start values on the caller's stream.
-int static_scratch(int device, cudaStream_t st, StaticScratchState* out) {
-    std::lock_guard<std::mutex> lock(g_static_mu);
-    if (device < 0 || device >= kMaxDevices) {
-        set_error("abft_verify_noalloc: device index out of range");
-        return ABFT_ERR_ARG;
-    }
-    StaticScratchState& s = g_static[device];
-    if (!s.ready) {
+// Unique id of the calling thread's current context (0 when unavailable).
+unsigned long long current_context_id() {
+    static std::once_flag once;
+    static PFN_cuCtxGetCurrent_v4000 get_current = nullptr;
+    static PFN_cuCtxGetId_v12000 get_id = nullptr;
+    std::call_once(once, [] {
         void* p = nullptr;
-        cudaError_t e = cudaGetSymbolAddress(&p, g_verify_scratch);
-        if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(verify scratch)");
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
+        p = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<PFN_cuCtxGetId_v12000>(p);
+        (void)cudaGetLastError();
+    });
+    CUcontext ctx = nullptr;
+    unsigned long long id = 0;
+    if (get_current && get_id && get_current(&ctx) == CUDA_SUCCESS && ctx != nullptr &&
+        get_id(ctx, &id) == CUDA_SUCCESS)
+        return id;
+    return 0;
+}
+
+// Set-up once per context, with the caller's device current: resolve the
+// device address of the static array (host code may not use the symbol
+// itself; cudaGetSymbolAddress also makes the runtime's context current) and
+// bring the array to its start values on the caller's stream.
+int static_scratch(int device, cudaStream_t st, StaticScratchState* out) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_verify_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(verify scratch)");
+    const unsigned long long ctx = current_context_id();
+    const auto key = std::make_pair(ctx != 0 ? ctx : (unsigned long long)device | (1ull << 63),
+                                    reinterpret_cast<uintptr_t>(p));
+    std::lock_guard<std::mutex> lock(g_static_mu);
+    auto it = g_static.find(key);
+    if (it == g_static.end()) {
+        StaticScratchState s;
         e = cudaMemsetAsync(p, 0, kStaticScratchBytes, st);
         if (e == cudaSuccess) e = cudaMemsetAsync(static_cast<unsigned char*>(p) + 48 * 1024, 0xff, 16 * 1024, st);
         if (e == cudaSuccess) e = cudaDeviceGetAttribute(&s.sms, cudaDevAttrMultiProcessorCount, device);
         if (e != cudaSuccess) return cuda_fail(e, "verify scratch set-up");
         s.base = static_cast<unsigned char*>(p);
-        s.ready = true;
+        it = g_static.emplace(key, s).first;
     }
-    *out = s;
+    *out = it->second;
     return ABFT_OK;
 }
 
@@ -1436,6 +1484,11 @@ int set_verify_kernel(int which) {
 
 int verify_kernel() { return g_verify_kernel.load(std::memory_order_relaxed); }
 
+int set_wait_limit(int polls) {
+    if (polls < 0) return -1;
+    return g_wait_limit.exchange(polls);
+}
+
 int launch_verify_static(const float* Cf, int64_t ldc, int M, int N, const double* expv, double tau, int injected,
                          int* errcol, double* rowdiff, int* cm, cudaStream_t st) {
     if (N > kStaticMaxCols) {
@@ -1454,23 +1507,23 @@ int launch_verify_static(const float* Cf, int64_t ldc, int M, int N, const doubl
     w.vacc_t = reinterpret_cast<float*>(s.base + 32 * 1024);
     w.vacc_m = reinterpret_cast<uint32_t*>(s.base + 48 * 1024);
     w.vact = reinterpret_cast<double*>(s.base + 64 * 1024);
+    w.vd = reinterpret_cast<double*>(s.base + 96 * 1024);
+    w.vw = reinterpret_cast<double*>(s.base + 128 * 1024);
     w.vcnt = reinterpret_cast<int*>(s.base + kStaticColBytes);
     w.rec = reinterpret_cast<FragRecord*>(s.base + kStaticColBytes + 256);
     w.ctr = reinterpret_cast<Counters*>(s.base + kStaticColBytes + 512);
     const bool vec = aligned16(Cf) && (ldc % 4 == 0) && (N % 4 == 0);
-    const int reduce_bytes = kWarps * kGroupCols * 16;
-    const int smem = std::max(reduce_bytes, 16 * N);  // d / w always fit: N <= kStaticMaxCols
+    const int smem = kWarps * kGroupCols * 16;
     const int per_sm = resident_per_sm(vec ? (const void*)k_verify<true> : (const void*)k_verify<false>, smem);
     int groups, chunks, rows_per;
     verify_geometry(per_sm * s.sms, M, N, groups, chunks, rows_per);
     dim3 grid(groups, chunks);
-    const int total = groups * chunks;
     if (vec)
-        k_verify<true><<<grid, kThreads, smem, st>>>(Cf, ldc, M, N, rows_per, total, 1, expv, tau, injected, 0, 1,
-                                                     -1, w, nullptr, nullptr, 0, 0.f, 0, nullptr, 0);
+        k_verify<true><<<grid, kThreads, smem, st>>>(Cf, ldc, M, N, rows_per, expv, tau, injected, 0, 1, -1, w,
+                                                     nullptr, nullptr, 0, 0.f, 0, nullptr, 0);
     else
-        k_verify<false><<<grid, kThreads, smem, st>>>(Cf, ldc, M, N, rows_per, total, 1, expv, tau, injected, 0, 1,
-                                                      -1, w, nullptr, nullptr, 0, 0.f, 0, nullptr, 0);
+        k_verify<false><<<grid, kThreads, smem, st>>>(Cf, ldc, M, N, rows_per, expv, tau, injected, 0, 1, -1, w,
+                                                      nullptr, nullptr, 0, 0.f, 0, nullptr, 0);
     if (int rc = check_launch("verify (static scratch)")) return rc;
     k_static_copyout<<<1, 32, 0, st>>>(w.rec, w.ctr, errcol, rowdiff, cm);
     return check_launch("verify copy-out");

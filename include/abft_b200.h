@@ -160,11 +160,14 @@ int abft_calibrate(abft_ws* ws, const float* dC, int64_t ldc, int f, double* dDi
  * caller passes everything: the fragment dC_frag (M x N, leading dimension
  * ldc), its expected row dExpRow[N] (e.g. from abft_encode), and the outputs
  * dErrCol (int), dRowDiff (double) and dCM (int[4], TP TN FP FN, incremented).
- * Scratch is a static device array inside this library, held by every GPU that
- * loads it until the process exits, limited to N <= 4096 columns (larger N
- * returns ABFT_ERR_ARG). The first call on a device sets that array up (it
+ * Scratch is a static device array inside this library (about 161 KB), held
+ * by every GPU that loads it until the process exits, limited to N <= 4096
+ * columns (larger N returns ABFT_ERR_ARG). The array exists once per CUDA
+ * context - normally once per device, in the runtime's primary context; a
+ * second context on a device, or the one that follows cudaDeviceReset, has
+ * its own copy. The first call in a context sets that context's copy up (it
  * looks up the array's device address and clears it on `stream`); make that
- * first call before any stream capture. All calls on a device share the
+ * first call before any stream capture. All calls in a context share the
  * array: calls whose work overlaps on the GPU race; calls ordered one after
  * another (same stream, or synchronised) are safe. No cudaMalloc, cudaFree or
  * allocating library routine is called. */
@@ -182,6 +185,17 @@ int abft_verify_noalloc(const float* dC_frag, int64_t ldc, int M, int N, const d
 #define ABFT_VERIFY_LDG 1
 #define ABFT_VERIFY_TMA 2
 int abft_set_verify_kernel(int which);
+
+/* Polls each wait of the TMA verify body makes for one bulk tensor copy
+ * before it gives up (default 1048576). No counterpart in the reference, whose
+ * kernels never wait on a copy. A wait that gives up marks the launch void:
+ * the kernel waits (with the default limit) for the copies it issued, adds
+ * nothing, finishes its arrival protocol and returns, and the next
+ * abft_ws_read_counters returns ABFT_ERR_CUDA with a message that names the
+ * wait; the context stays usable. Meant for tests of that failure path (0
+ * makes every such wait give up at once). Process-wide; returns the previous
+ * limit, or ABFT_ERR_ARG for a negative one. */
+int abft_set_wait_limit(int polls);
 
 /* Localise and correct fragment f, gated on the device by the verify result:
  * replaces launch_localize_correct (kernels/abft_stepwise.cuh:218-239).

@@ -82,3 +82,40 @@ def test_noalloc_rejects_wide_fragments(abft):
                                       ctypes.c_void_p(cm.data_ptr()), None)
     assert rc == abft._lib.ABFT_ERR_ARG
     assert "4096" in abft._lib.last_error()
+
+
+def test_noalloc_width_changes_match_oracle(abft, orc):
+    """Calls of different widths in a row (a narrow fragment, the full
+    4096-column maximum, the narrow one again) each start from clean scratch:
+    every result equals the oracle's decision directly (errcol, rowdiff bits,
+    confusion-matrix increment)."""
+    M, K, N = 384, 96, 4096
+    A, B = tiles(orc, M, K, N, 81, 82)
+    C0 = product_f64(A, B)
+    expRow = orc.expected_row(orc.col_checksum_A(A), B)
+    exp_dev = torch.from_numpy(expRow).cuda()
+    tau = 1e-5 * K
+    cases = [
+        # (column offset, width, fault (row, column, delta) or None, tau, injected)
+        (128, 200, (10, 128 + 57, 2.0), tau, True),
+        (0, 4096, (300, 4000, -5.0), tau, True),
+        (128, 200, None, tau, False),
+        (0, 4096, None, 0.0, False),     # tau = 0: the arg-max over rounding noise of every column
+        (128, 200, (17, 128 + 3, 0.5), tau, True),
+    ]
+    out_ec = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out_rd = torch.zeros(1, dtype=torch.float64, device="cuda")
+    out_cm = torch.zeros(4, dtype=torch.int32, device="cuda")
+    want_cm = np.zeros(4, np.int64)
+    for off, nf, fault, t, injected in cases:
+        C = C0 if fault is None else add_fault(C0, fault[0], fault[1], fault[2])
+        dC = torch.from_numpy(np.ascontiguousarray(C)).cuda()
+        call_noalloc(abft, dC, off, nf, exp_dev, t, injected, out_ec, out_rd, out_cm)
+        torch.cuda.synchronize()
+        w_ec, w_rd, w_cm = orc.detect_row(expRow[off:off + nf], orc.actual_row(C[:, off:off + nf]), t, injected)
+        want_cm += w_cm
+        assert int(out_ec.item()) == w_ec, (off, nf, fault)
+        assert np.float64(out_rd.item()).view(np.uint64) == np.float64(w_rd).view(np.uint64)
+        assert out_cm.cpu().numpy().tolist() == want_cm.tolist()
+        if fault is not None:
+            assert w_ec == fault[1] - off
