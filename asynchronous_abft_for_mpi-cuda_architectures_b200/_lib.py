@@ -134,6 +134,7 @@ SIGNATURES = {
     "abft_session_set_golden": (_I, [_P, _P, _I64]),
     "abft_session_encode": (_I, [_P, _DP]),
     "abft_session_baseline": (_I, [_P, _I, _I, _DP, _DP]),
+    "abft_session_baseline_monolithic": (_I, [_P, _I, _I, _DP, _DP]),
     "abft_session_online": (_I, [_P, ctypes.POINTER(OnlineArgs), ctypes.POINTER(OnlineResult)]),
     "abft_session_read_injections": (_I, [_P, _I, _IP, ctypes.POINTER(ctypes.c_float)]),
     "abft_session_run_host": (_I, [_P, _P, _P, _P, ctypes.POINTER(OnlineArgs), ctypes.POINTER(OnlineResult),

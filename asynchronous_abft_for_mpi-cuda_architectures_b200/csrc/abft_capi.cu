@@ -48,7 +48,7 @@ WsLayout ws_layout(int M_b, int N_b, int K, int F, int nfmax, int max_iters) {
     L.vact = take(sizeof(double) * nfpad);
     L.vd = take(sizeof(double) * nfpad);
     L.vw = take(sizeof(double) * nfpad);
-    L.vcnt = take(sizeof(int) * (kArriveGroup + groups));
+    L.vcnt = take(sizeof(int) * vcnt_ints((int)groups));
     L.lact = take(sizeof(double) * M_b);
     L.ld = take(sizeof(double) * M_b);
     L.lw = take(sizeof(double) * M_b);

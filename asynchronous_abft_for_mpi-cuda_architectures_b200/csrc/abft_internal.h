@@ -14,13 +14,17 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kGroupCols = 128;  // columns per verify CTA: 32 lanes x 4 columns
 constexpr int kMaxChunks = 1024; // row chunks per column group (verify grid.y)
 constexpr int kVerifySmemMax = 64 * 1024;  // verify dynamic shared memory cap
-// Arrival state of one verify launch, in WsDev::vcnt (all zero between launches):
-//   [kArriveFinal]      column groups that have finished (the last one decides the fragment)
-//   [kArriveCand]       set when some group holds a column whose |actual - expected| may exceed tau
-//   [kArriveGroup + g]  CTAs of column group g that have finished (the last one finishes the group)
-constexpr int kArriveFinal = 0;
-constexpr int kArriveCand = 1;
+// Arrival and work state of one verify launch, in WsDev::vcnt (all zero
+// between launches; G = number of column groups):
+//   [0, 2)                  one 64-bit word: column groups that have finished (low
+//                           half; the last one decides the fragment) and, in the
+//                           high half, how many of them hold a column whose
+//                           |actual - expected| may exceed tau
+//   [kArriveGroup + g]      CTAs of column group g that have finished (the last one
+//                           finishes the group)
+//   [kArriveGroup + G + g]  next unit of rows of column group g to hand out
 constexpr int kArriveGroup = 2;
+constexpr int vcnt_ints(int groups) { return kArriveGroup + 2 * groups; }
 
 // Per-fragment decision record (the reference's dErrCol[f] / dRowDiff[f],
 // plus the located row).
@@ -78,7 +82,7 @@ struct WsDev {
     double* vact;      // [nfpad]
     double* vd;
     double* vw;
-    int* vcnt;         // [kArriveGroup + groups_max]
+    int* vcnt;         // [vcnt_ints(groups_max)], 8-byte aligned
     double* lact;      // [M_b]
     double* ld;
     double* lw;

@@ -301,17 +301,19 @@ __device__ __forceinline__ double ld_sel(const double* p) {
 // Arg-max of k_detect_row / k_locate_correct (kernels/abft_stepwise.cuh:85-110,
 // :174-187) over n entries, run by one 256-thread CTA. act/dd/ww hold the fast
 // sum, its |act - exp| and window; entries that could change the outcome are
-// first re-summed exactly by `exact(j)` (warp-cooperative). Returns the
+// first re-summed exactly by `exact(j)` (warp-cooperative). Entries with
+// live(j) false are known to be at most tau and are not read. Returns the
 // reference's winner or -1.
-template <bool CG, class Exact>
+template <bool CG, class Exact, class Live>
 __device__ int final_select(int n, double tau, const double* __restrict__ expv, double* act, double* dd, double* ww,
-                            Exact exact, SelectSmem& sm) {
+                            Exact exact, Live live, SelectSmem& sm) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     // Pass 1: largest certified candidate; is there any candidate at all, any uncertified one?
     double bc = -INFINITY;
     int anyc = 0, anyu = 0;
 #pragma unroll 4
     for (int j = tid; j < n; j += kThreads) {
+        if (!live(j)) continue;
         const double wv = ld_sel<CG>(ww + j), dv = ld_sel<CG>(dd + j);
         if (wv == 0.0 && dv > tau && dv > bc) bc = dv;
         if (dv + wv > tau) {
@@ -336,6 +338,7 @@ __device__ int final_select(int n, double tau, const double* __restrict__ expv, 
             __syncthreads();
 #pragma unroll 4
             for (int j = tid; j < n; j += kThreads) {
+                if (!live(j)) continue;
                 const double wv = ld_sel<CG>(ww + j);
                 if (wv != 0.0) {
                     const double hi = ld_sel<CG>(dd + j) + wv;
@@ -369,7 +372,7 @@ __device__ int final_select(int n, double tau, const double* __restrict__ expv, 
     int bj = -1;
 #pragma unroll 4
     for (int j = tid; j < n; j += kThreads) {
-        if (ld_sel<CG>(ww + j) == 0.0) {
+        if (live(j) && ld_sel<CG>(ww + j) == 0.0) {
             const double dv = ld_sel<CG>(dd + j);
             if (dv > tau && dv > best) {
                 best = dv;
@@ -495,36 +498,46 @@ __device__ __forceinline__ void verify_tail(unsigned char* dsm, SelectSmem& sel,
         if (tid < kGroupCols && col < N && wv == 0.0) calib_out[col] = d;
         cand = 0;
     }
-    fence_acq_rel_gpu();
+    // With at most 32 groups the final word's high half is a mask of the
+    // groups that voted yes, and only those are read by the decision: a group
+    // that votes no needs no fence before its arrival (the common case). With
+    // more groups it holds a count, and every group fences.
+    const bool mask_mode = gridDim.x <= 32u;
     cand = __syncthreads_or(cand);
+    if (cand || !mask_mode) {
+        fence_acq_rel_gpu();  // this group's act / d / w before its arrival
+        __syncthreads();
+    }
     if (tid == 0) {
-        w.vcnt[kArriveGroup + g] = 0;  // every CTA of the group has arrived
-        if (cand) atomicOr(w.vcnt + kArriveCand, 1);
-        fence_acq_rel_gpu();
-        sel.flag = (atomicAdd(w.vcnt + kArriveFinal, 1) == (int)gridDim.x - 1);
+        // every CTA of the group has arrived: its counters go back to zero
+        w.vcnt[kArriveGroup + g] = 0;
+        w.vcnt[kArriveGroup + gridDim.x + g] = 0;
+        unsigned long long vote = 0ull;
+        if (cand) vote = mask_mode ? (1ull << (32 + g)) : (1ull << 32);
+        // one atomic both counts this group and carries its vote
+        unsigned long long* fin = reinterpret_cast<unsigned long long*>(w.vcnt);
+        const unsigned long long old = atomicAdd(fin, 1ull + vote);
+        sel.flag = ((unsigned)old == gridDim.x - 1u);
+        sel.cnt = (int)((old + vote) >> 32);  // vote mask (or count), this group included
     }
     __syncthreads();
     if (!sel.flag) return;
     fence_acq_rel_gpu();
 
     // Last group: the fragment's decision.
-    if (tid == 0) sel.cnt = __ldcg(w.vcnt + kArriveCand);
-    __syncthreads();
-    const int any = sel.cnt;
+    const unsigned votes = (unsigned)sel.cnt;
     __syncthreads();
     if (calib_out != nullptr) {
-        if (tid == 0) {
-            w.vcnt[kArriveFinal] = 0;
-            w.vcnt[kArriveCand] = 0;
-        }
+        if (tid == 0) *reinterpret_cast<unsigned long long*>(w.vcnt) = 0ull;
         return;
     }
     // The reference's detection (k_detect_row) on exact values; a fragment in
     // which no column can exceed tau has no winner.
     int ec = -1;
-    if (any)
-        ec = final_select<true>(N, tau, expv, w.vact, w.vd, w.vw,
-                                [&](int j) { return exact_chain(C + j, ldc, M); }, sel);
+    if (votes != 0u)
+        ec = final_select<true>(
+            N, tau, expv, w.vact, w.vd, w.vw, [&](int j) { return exact_chain(C + j, ldc, M); },
+            [&](int j) { return !mask_mode || ((votes >> (j / kGroupCols)) & 1u) != 0u; }, sel);
     if (tid == 0) {
         const double rd = (ec >= 0) ? (__ldcg(w.vact + ec) - expv[ec]) : 0.0;
         w.rec[f].errcol = ec;
@@ -542,52 +555,58 @@ __device__ __forceinline__ void verify_tail(unsigned char* dsm, SelectSmem& sel,
             L.errrow = -1;
             L.rowdiff = rd;
         }
-        w.vcnt[kArriveFinal] = 0;
-        w.vcnt[kArriveCand] = 0;
+        *reinterpret_cast<unsigned long long*>(w.vcnt) = 0ull;
     }
 }
 
 
 // Fused actualRow + detect for one fragment (M x N, leading dimension ldc).
-// grid = (groups of 128 columns, row chunks). Each CTA streams its tile with
-// 128-bit loads, reduces it to per-column (sum, |x|-sum, smallest |x|) and
-// adds those into per-column accumulators with device atomics (any order:
-// certified sums are exact in every order, uncertified ones carry a window
-// valid for every order). The last CTA to finish certifies each column and
-// runs the reference's arg-max. Shared memory: 16 KB for the CTA reduction,
-// reused by the last CTA for the d / w arrays when 16*N bytes fit.
+// grid = (groups of 128 columns, CTAs per group). A column group's rows are
+// cut into units of unit_rows rows (a multiple of kBatch * kWarps): CTA y of
+// the group takes unit y first, then one thread fetches the index of the CTA's
+// next unit from the group's counter while the current unit streams, so CTAs
+// that get less bandwidth take fewer units and the group's CTAs finish within
+// about one unit of each other (a CTA-level grab keeps the counter at a few
+// atomics per microsecond). Each thread streams 4 columns with 128-bit loads
+// and keeps per-column (sum, |x|-sum, smallest |x|); the CTA adds those into
+// per-column accumulators with device atomics (any order: certified sums are
+// exact in every order, uncertified ones carry a window valid for every
+// order); the tail finishes the columns and the decision. Shared memory:
+// 16 KB for the CTA's fold.
 template <bool VEC>
 __global__ void __launch_bounds__(kThreads, 4)
-    k_verify(const float* __restrict__ C, long long ldc, int M, int N, int rows_per, const double* __restrict__ expv, double tau, int injected, int f, int F, int it, WsDev w,
-             float* Cw, const InjectPlan* __restrict__ plan, int plan_it, float add_delta, int log_inj,
-             double* calib_out, cudaGraphConditionalHandle cond) {
+    k_verify(const float* __restrict__ C, long long ldc, int M, int N, int unit_rows, const double* __restrict__ expv,
+             double tau, int injected, int f, int F, int it, WsDev w, float* Cw, const InjectPlan* __restrict__ plan,
+             int plan_it, float add_delta, int log_inj, double* calib_out, cudaGraphConditionalHandle cond) {
     extern __shared__ __align__(16) unsigned char dsm[];
     __shared__ SelectSmem sel;
+    __shared__ int s_next[2];
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int g = blockIdx.x, chunk = blockIdx.y;
+    const int g = blockIdx.x;
     const int c0 = g * kGroupCols + lane * 4;
-    const int r0 = chunk * rows_per;
-    const int r1 = min(M, r0 + rows_per);
+    const int nunits = (M + unit_rows - 1) / unit_rows;
+    int* const next_unit = w.vcnt + kArriveGroup + gridDim.x + g;
 
     // The expected checksums of this group's columns (1 KB) are read only by
-    // the last CTA; the first row chunk pulls them into L2 meanwhile.
-    if (chunk == 0 && tid < kGroupCols / 16 && g * kGroupCols + tid * 16 < N)
+    // the group's last CTA; the group's first CTA pulls them into L2 meanwhile.
+    if (blockIdx.y == 0 && tid < kGroupCols / 16 && g * kGroupCols + tid * 16 < N)
         prefetch_l2(expv + g * kGroupCols + tid * 16);
 
     double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
     float t0 = 0.f, t1 = 0.f, t2 = 0.f, t3 = 0.f;
     uint32_t m0 = kFull, m1 = kFull, m2 = kFull, m3 = kFull;
 
-    // Graph mode: this iteration's planned fault is applied here, by the one
-    // thread whose loads cover the element (nothing reads C between the SGEMM
-    // and this kernel, so the result equals injecting on the compute stream).
+    // Graph mode: this iteration's planned fault is applied here, by the
+    // thread whose loads cover the element: warp (row mod kWarps) of whichever
+    // CTA takes the row's unit (nothing reads C between the SGEMM and this
+    // kernel, so the result equals injecting on the compute stream).
     int inj_row = -1, inj_k = 0, inj_bit = -1;
     if (plan != nullptr) {
         const InjectPlan p = plan[plan_it];
         injected = (p.frag == f) ? 1 : 0;
-        if (injected && p.row >= r0 && p.row < r1 && ((p.row - r0) % kWarps) == warp && p.col >= c0 &&
-            p.col < c0 + 4 && p.col < N) {
+        if (injected && p.row >= 0 && p.row < M && (p.row % kWarps) == warp && p.col >= c0 && p.col < c0 + 4 &&
+            p.col < N) {
             inj_row = p.row;
             inj_k = p.col - c0;
             inj_bit = p.bit;
@@ -615,41 +634,54 @@ __global__ void __launch_bounds__(kThreads, 4)
         acc1(v.w, s3, t3, m3);
     };
 
-    // Batches of kBatch rows per warp, predicated, so that every load of a
-    // batch is in flight at once (one memory latency per batch).
-    for (int r = r0 + warp; r < r1; r += kBatch * kWarps) {
-        float4 v[kBatch];
+    int u = blockIdx.y;
+    int nxt = 0;
+    if (tid == 0 && u < nunits) nxt = (int)gridDim.y + atomicAdd(next_unit, 1);
+    for (int i = 0; u < nunits; ++i) {
+        const int r1 = min(M, (u + 1) * unit_rows);
+        // Batches of kBatch rows per warp (rows warp, warp + kWarps, ...),
+        // predicated, so that every load of a batch is in flight at once.
+        for (int r = u * unit_rows + warp; r < r1; r += kBatch * kWarps) {
+            float4 v[kBatch];
 #pragma unroll
-        for (int u = 0; u < kBatch; ++u) {
-            const int rr = r + u * kWarps;
-            v[u] = (rr < r1) ? load(rr) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-        if (inj_row >= 0) {
+            for (int k = 0; k < kBatch; ++k) {
+                const int rr = r + k * kWarps;
+                v[k] = (rr < r1) ? load(rr) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+            if (inj_row >= 0) {
 #pragma unroll
-            for (int u = 0; u < kBatch; ++u) {
-                if (r + u * kWarps == inj_row) {
-                    const float before = inj_k == 0 ? v[u].x : inj_k == 1 ? v[u].y : inj_k == 2 ? v[u].z : v[u].w;
-                    const float after = (inj_bit < 0) ? __fadd_rn(before, add_delta)
-                                                      : __uint_as_float(__float_as_uint(before) ^ (1u << inj_bit));
-                    if (inj_k == 0) v[u].x = after;
-                    else if (inj_k == 1) v[u].y = after;
-                    else if (inj_k == 2) v[u].z = after;
-                    else v[u].w = after;
-                    Cw[(long long)inj_row * ldc + c0 + inj_k] = after;
-                    if (log_inj) {
-                        InjectLog& L = w.ilog[plan_it];
-                        L.frag = f;
-                        L.row = inj_row;
-                        L.col = c0 + inj_k;
-                        L.bit = inj_bit;
-                        L.before = before;
-                        L.after = after;
+                for (int k = 0; k < kBatch; ++k) {
+                    if (r + k * kWarps == inj_row) {
+                        const float before = inj_k == 0 ? v[k].x : inj_k == 1 ? v[k].y : inj_k == 2 ? v[k].z : v[k].w;
+                        const float after = (inj_bit < 0)
+                                                ? __fadd_rn(before, add_delta)
+                                                : __uint_as_float(__float_as_uint(before) ^ (1u << inj_bit));
+                        if (inj_k == 0) v[k].x = after;
+                        else if (inj_k == 1) v[k].y = after;
+                        else if (inj_k == 2) v[k].z = after;
+                        else v[k].w = after;
+                        Cw[(long long)inj_row * ldc + c0 + inj_k] = after;
+                        if (log_inj) {
+                            InjectLog& L = w.ilog[plan_it];
+                            L.frag = f;
+                            L.row = inj_row;
+                            L.col = c0 + inj_k;
+                            L.bit = inj_bit;
+                            L.before = before;
+                            L.after = after;
+                        }
                     }
                 }
             }
-        }
 #pragma unroll
-        for (int u = 0; u < kBatch; ++u) acc(v[u]);
+            for (int k = 0; k < kBatch; ++k) acc(v[k]);
+        }
+        // the next unit (fetched during this one) for every thread; slot i & 1
+        // is written again only after the next barrier
+        if (tid == 0) s_next[i & 1] = nxt;
+        __syncthreads();
+        u = s_next[i & 1];
+        if (tid == 0 && u < nunits) nxt = (int)gridDim.y + atomicAdd(next_unit, 1);
     }
 
     verify_tail(dsm, sel, true, s0, s1, s2, s3, t0, t1, t2, t3, m0, m1, m2, m3, C, ldc, M, N, expv, tau, injected, f,
@@ -888,7 +920,8 @@ __global__ void __launch_bounds__(kThreads)
     fence_acq_rel_gpu();
 
     const int er = final_select<true>(
-        M, tau, expc, w.lact, w.ld, w.lw, [&](int i) { return exact_chain(C + (long long)i * ldc, 1, N); }, sel);
+        M, tau, expc, w.lact, w.ld, w.lw, [&](int i) { return exact_chain(C + (long long)i * ldc, 1, N); },
+        [](int) { return true; }, sel);
     if (tid == 0) {
         *w.lcnt = 0;
         const double rd = __ldcg(&w.rec[f].rowdiff);
@@ -1130,19 +1163,21 @@ int check_launch(const char* what) {
     return ABFT_OK;
 }
 
-// Verify geometry: column groups x row chunks, sized to one full wave of
+// Verify geometry: column groups x CTAs per group, sized to one full wave of
 // resident CTAs (target = resident CTAs per SM x SMs; a second, mostly empty
-// wave would double the launch time).
-void verify_geometry(int target, int M, int N, int& groups, int& chunks, int& rows_per) {
+// wave would double the launch time). A unit of rows is at least two batches
+// per warp (2 * kBatch * kWarps = 128 rows: measured on B200, one-batch units
+// lose more to the per-unit barrier than they gain in balance) and about
+// 1/kUnitsPerCta of a CTA's share; a group has no more CTAs than units (this
+// bounds the atomics per accumulator to M / 128).
+constexpr int kUnitsPerCta = 16;
+void verify_geometry(int target, int M, int N, int& groups, int& chunks, int& unit_rows) {
+    constexpr int kUnit = kBatch * kWarps;
     groups = (N + kGroupCols - 1) / kGroupCols;
-    chunks = target / groups;
-    if (chunks < 1) chunks = 1;
-    if (chunks > kMaxChunks) chunks = kMaxChunks;
-    rows_per = (M + chunks - 1) / chunks;
-    rows_per = ((rows_per + kWarps - 1) / kWarps) * kWarps;
-    // at least one full batch per warp: bounds the atomics per accumulator to M / 64
-    rows_per = std::max(rows_per, kBatch * kWarps);
-    chunks = (M + rows_per - 1) / rows_per;
+    chunks = std::min(std::max(target / groups, 1), kMaxChunks);
+    unit_rows = kUnit * std::max(2, M / (chunks * kUnit * kUnitsPerCta));
+    const int units = (M + unit_rows - 1) / unit_rows;
+    chunks = std::min(chunks, units);
 }
 
 // Geometry of the TMA-staged verify: as above, with row chunks a multiple of
@@ -1291,7 +1326,7 @@ int launch_verify(abft_ws* ws, const float* dC, int64_t ldc, int f, double tau, 
     if (it >= ws->max_iters) it = -1;
     const InjectPlan* plan = (plan_it >= 0) ? ws->d.plan : nullptr;
     float* Cw = const_cast<float*>(Cf);
-    int groups, chunks, rows_per;
+    int groups, chunks;
 
     // TMA-staged body: 16-byte aligned fragment, pitch a multiple of 4 floats,
     // at least one full box; by default for fragments of kTmaMinBytes or more.
@@ -1301,6 +1336,7 @@ int launch_verify(abft_ws* ws, const float* dC, int64_t ldc, int f, double tau, 
     CUtensorMap map;
     if (tma_ok && want_tma && fragment_tensor_map(&map, Cf, ldc, M, N)) {
         const int per_sm = resident_per_sm((const void*)k_verify_tma, kTmaSmem + kTmaAlign);
+        int rows_per;
         verify_geometry_tma(per_sm * ws->sms, M, N, groups, chunks, rows_per);
         k_verify_tma<<<dim3(groups, chunks), kThreads, kTmaSmem + kTmaAlign, st>>>(
             map, Cf, ldc, M, N, rows_per, expv, tau, injected, f, ws->F, it, ws->d, Cw, plan, plan_it, add_delta,
@@ -1312,13 +1348,14 @@ int launch_verify(abft_ws* ws, const float* dC, int64_t ldc, int f, double tau, 
     // 16 KB of shared memory per CTA: the fold of its eight warps' partials
     const int smem = kWarps * kGroupCols * 16;
     const int per_sm = resident_per_sm(vec ? (const void*)k_verify<true> : (const void*)k_verify<false>, smem);
-    verify_geometry(per_sm * ws->sms, M, N, groups, chunks, rows_per);
+    int unit_rows;
+    verify_geometry(per_sm * ws->sms, M, N, groups, chunks, unit_rows);
     dim3 grid(groups, chunks);
     if (vec)
-        k_verify<true><<<grid, kThreads, smem, st>>>(Cf, ldc, M, N, rows_per, expv, tau, injected, f, ws->F, it,
+        k_verify<true><<<grid, kThreads, smem, st>>>(Cf, ldc, M, N, unit_rows, expv, tau, injected, f, ws->F, it,
                                                      ws->d, Cw, plan, plan_it, add_delta, log_inj, calib_out, cond);
     else
-        k_verify<false><<<grid, kThreads, smem, st>>>(Cf, ldc, M, N, rows_per, expv, tau, injected, f, ws->F, it,
+        k_verify<false><<<grid, kThreads, smem, st>>>(Cf, ldc, M, N, unit_rows, expv, tau, injected, f, ws->F, it,
                                                       ws->d, Cw, plan, plan_it, add_delta, log_inj, calib_out, cond);
     return check_launch("verify");
 }
@@ -1384,8 +1421,8 @@ int launch_inject(float* dC, int64_t ldc, int row, int col, int mode, float delt
 //   [64 KiB, 96 KiB)    per-column final sums          (double[4096])
 //   [96 KiB, 128 KiB)   per-column |actual - expected| (double[4096])
 //   [128 KiB, 160 KiB)  per-column windows             (double[4096])
-//   then the arrival counters (2 + 32 ints), one decision record and one
-//   counter block, 256 bytes each.
+//   then the arrival and work counters (2 + 2 x 32 ints, 512 bytes), one
+//   decision record and one counter block (256 bytes each).
 // Every call in a CUDA context shares that context's copy of the array. The
 // kernel's last CTAs put the accumulators and the arrival counters back to
 // their start values, and the copy-out kernel zeroes the counter block, so
@@ -1396,8 +1433,9 @@ namespace {
 
 constexpr int kStaticMaxCols = 4096;
 constexpr size_t kStaticColBytes = 160 * 1024;
-constexpr size_t kStaticScratchBytes = kStaticColBytes + 3 * 256;
-static_assert(sizeof(int) * (kArriveGroup + kStaticMaxCols / kGroupCols) <= 256, "arrival counters");
+constexpr size_t kStaticCounterBytes = 512;
+constexpr size_t kStaticScratchBytes = kStaticColBytes + kStaticCounterBytes + 2 * 256;
+static_assert(sizeof(int) * vcnt_ints(kStaticMaxCols / kGroupCols) <= kStaticCounterBytes, "verify counters");
 static __device__ __align__(256) unsigned char g_verify_scratch[kStaticScratchBytes];
 
 struct StaticScratchState {
@@ -1510,19 +1548,19 @@ int launch_verify_static(const float* Cf, int64_t ldc, int M, int N, const doubl
     w.vd = reinterpret_cast<double*>(s.base + 96 * 1024);
     w.vw = reinterpret_cast<double*>(s.base + 128 * 1024);
     w.vcnt = reinterpret_cast<int*>(s.base + kStaticColBytes);
-    w.rec = reinterpret_cast<FragRecord*>(s.base + kStaticColBytes + 256);
-    w.ctr = reinterpret_cast<Counters*>(s.base + kStaticColBytes + 512);
+    w.rec = reinterpret_cast<FragRecord*>(s.base + kStaticColBytes + kStaticCounterBytes);
+    w.ctr = reinterpret_cast<Counters*>(s.base + kStaticColBytes + kStaticCounterBytes + 256);
     const bool vec = aligned16(Cf) && (ldc % 4 == 0) && (N % 4 == 0);
     const int smem = kWarps * kGroupCols * 16;
     const int per_sm = resident_per_sm(vec ? (const void*)k_verify<true> : (const void*)k_verify<false>, smem);
-    int groups, chunks, rows_per;
-    verify_geometry(per_sm * s.sms, M, N, groups, chunks, rows_per);
+    int groups, chunks, unit_rows;
+    verify_geometry(per_sm * s.sms, M, N, groups, chunks, unit_rows);
     dim3 grid(groups, chunks);
     if (vec)
-        k_verify<true><<<grid, kThreads, smem, st>>>(Cf, ldc, M, N, rows_per, expv, tau, injected, 0, 1, -1, w,
+        k_verify<true><<<grid, kThreads, smem, st>>>(Cf, ldc, M, N, unit_rows, expv, tau, injected, 0, 1, -1, w,
                                                      nullptr, nullptr, 0, 0.f, 0, nullptr, 0);
     else
-        k_verify<false><<<grid, kThreads, smem, st>>>(Cf, ldc, M, N, rows_per, expv, tau, injected, 0, 1, -1, w,
+        k_verify<false><<<grid, kThreads, smem, st>>>(Cf, ldc, M, N, unit_rows, expv, tau, injected, 0, 1, -1, w,
                                                       nullptr, nullptr, 0, 0.f, 0, nullptr, 0);
     if (int rc = check_launch("verify (static scratch)")) return rc;
     k_static_copyout<<<1, 32, 0, st>>>(w.rec, w.ctr, errcol, rowdiff, cm);

@@ -62,6 +62,8 @@ struct abft_session {
     InjectPlan* plan_host = nullptr;  // pinned, max_iters entries
     cudaGraphExec_t bexec = nullptr;  // graph of the baseline pass
     int b_repeats = -1;
+    cudaGraphExec_t mexec = nullptr;  // graph of the monolithic baseline pass
+    int m_repeats = -1;
     // run_host: copy stream, input arrivals (A, then B per fragment), final
     // fragments ready for the host
     cudaStream_t xfer = nullptr;
@@ -512,6 +514,7 @@ int abft_session_destroy(abft_session* s) {
     if (s->xout) cudaStreamSynchronize(s->xout);
     drop_graph(s);
     if (s->bexec) cudaGraphExecDestroy(s->bexec);
+    if (s->mexec) cudaGraphExecDestroy(s->mexec);
     if (s->plan_host) cudaFreeHost(s->plan_host);
     for (auto e : s->compute_done)
         if (e) cudaEventDestroy(e);
@@ -585,42 +588,52 @@ int abft_session_encode(abft_session* s, double* encode_ms) {
     return ABFT_OK;
 }
 
-int abft_session_baseline(abft_session* s, int repeats, int graph, double* device_ms, double* host_ms) {
-    if (!s || repeats < 0) {
-        set_error("abft_session_baseline: bad argument");
-        return ABFT_ERR_ARG;
-    }
-    const NvtxRange range(graph ? "abft baseline pass (graph)" : "abft baseline pass");
+namespace {
+
+// One unprotected pass into dC0 on the compute stream: repeats x (F fragment
+// SGEMMs, or one SGEMM of the whole tile), optionally replayed as a CUDA graph
+// captured once per repeats; device time by events on the compute stream.
+int baseline_pass(abft_session* s, int repeats, int graph, bool monolithic, double* device_ms, double* host_ms) {
     CK(cudaStreamSynchronize(s->compute));
-    if (graph && (!s->bexec || s->b_repeats != repeats)) {
-        if (s->bexec) cudaGraphExecDestroy(s->bexec);
-        s->bexec = nullptr;
-        CK(cudaStreamBeginCapture(s->compute, cudaStreamCaptureModeThreadLocal));
+    cudaGraphExec_t& exec = monolithic ? s->mexec : s->bexec;
+    int& captured = monolithic ? s->m_repeats : s->b_repeats;
+    auto enqueue = [&]() -> int {
         int rc = ABFT_OK;
-        for (int it = 0; it < repeats && rc == ABFT_OK; ++it)
-            for (int f = 0; f < s->F && rc == ABFT_OK; ++f) rc = sgemm_frag(s, s->dC[0], f);
+        for (int it = 0; it < repeats && rc == ABFT_OK; ++it) {
+            if (monolithic)
+                rc = abft_sgemm(s->handle, s->dA, (int)s->lda, s->dB, (int)s->ldb, s->dC[0], (int)s->ldc, s->M_b,
+                                s->N_b, s->K);
+            else
+                for (int f = 0; f < s->F && rc == ABFT_OK; ++f) rc = sgemm_frag(s, s->dC[0], f);
+        }
+        return rc;
+    };
+    if (graph && (!exec || captured != repeats)) {
+        if (exec) cudaGraphExecDestroy(exec);
+        exec = nullptr;
+        CK(cudaStreamBeginCapture(s->compute, cudaStreamCaptureModeThreadLocal));
+        int rc = enqueue();
         cudaGraph_t g = nullptr;
         cudaError_t e = cudaStreamEndCapture(s->compute, &g);
         if (rc == ABFT_OK && e != cudaSuccess) rc = cuda_fail(e, "cudaStreamEndCapture (baseline)");
         if (rc == ABFT_OK) {
-            e = cudaGraphInstantiate(&s->bexec, g, 0);
+            e = cudaGraphInstantiate(&exec, g, 0);
             if (e != cudaSuccess) {
-                s->bexec = nullptr;
+                exec = nullptr;
                 rc = cuda_fail(e, "cudaGraphInstantiate (baseline)");
             }
         }
         if (g) cudaGraphDestroy(g);
         (void)cudaGetLastError();
         if (rc != ABFT_OK) return rc;
-        s->b_repeats = repeats;
+        captured = repeats;
     }
     const auto h0 = std::chrono::high_resolution_clock::now();
     CK(cudaEventRecord(s->t0, s->compute));
     if (graph) {
-        CK(cudaGraphLaunch(s->bexec, s->compute));
+        CK(cudaGraphLaunch(exec, s->compute));
     } else {
-        for (int it = 0; it < repeats; ++it)
-            for (int f = 0; f < s->F; ++f) RC(sgemm_frag(s, s->dC[0], f));
+        RC(enqueue());
     }
     CK(cudaEventRecord(s->t1, s->compute));
     CK(cudaEventSynchronize(s->t1));
@@ -630,6 +643,26 @@ int abft_session_baseline(abft_session* s, int repeats, int graph, double* devic
     if (device_ms) *device_ms = ms;
     if (host_ms) *host_ms = std::chrono::duration<double, std::milli>(h1 - h0).count();
     return ABFT_OK;
+}
+
+}  // namespace
+
+int abft_session_baseline(abft_session* s, int repeats, int graph, double* device_ms, double* host_ms) {
+    if (!s || repeats < 0) {
+        set_error("abft_session_baseline: bad argument");
+        return ABFT_ERR_ARG;
+    }
+    const NvtxRange range(graph ? "abft baseline pass (graph)" : "abft baseline pass");
+    return baseline_pass(s, repeats, graph, false, device_ms, host_ms);
+}
+
+int abft_session_baseline_monolithic(abft_session* s, int repeats, int graph, double* device_ms, double* host_ms) {
+    if (!s || repeats < 0) {
+        set_error("abft_session_baseline_monolithic: bad argument");
+        return ABFT_ERR_ARG;
+    }
+    const NvtxRange range(graph ? "abft monolithic baseline (graph)" : "abft monolithic baseline");
+    return baseline_pass(s, repeats, graph, true, device_ms, host_ms);
 }
 
 int abft_session_online(abft_session* s, const abft_online_args* a, abft_online_result* r) {

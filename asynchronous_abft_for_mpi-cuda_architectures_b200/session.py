@@ -95,6 +95,14 @@ class OnlineSession:
                  ctypes.byref(hms))
         return dms.value, hms.value
 
+    def baseline_monolithic(self, repeats, graph=False):
+        """repeats x one unprotected SGEMM of the whole tile (no fragments); (device_ms, host_ms)."""
+        dms, hms = ctypes.c_double(), ctypes.c_double()
+        with torch.cuda.device(self.device):
+            call("abft_session_baseline_monolithic", self.handle, int(repeats), int(bool(graph)), ctypes.byref(dms),
+                 ctypes.byref(hms))
+        return dms.value, hms.value
+
     def _args(self, mode, zone, add_delta, base_seed, rank, repeats, correct, log, profile=False, graph=False,
               seed_scheme="reference"):
         if correct not in ("inloop", "drain"):

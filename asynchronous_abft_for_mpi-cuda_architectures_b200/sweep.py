@@ -21,6 +21,10 @@ import sys
 PKG_DIR = os.path.dirname(os.path.abspath(__file__))
 DRIVER = os.path.join(PKG_DIR, "abft_gemm")
 
+# torchrun's rendezvous port is chosen when a run starts (a port picked when
+# the list is built could be taken by then): this argument marks its place.
+PORT_ARG = "--master-port={port}"
+
 MODES = [("baseline", ["--baseline"]), ("online, no fault", ["--inject", "none"]),
          ("online, additive fault", ["--inject", "add"])]
 
@@ -47,7 +51,8 @@ def free_port():
 
 
 def commands(k, extra=()):
-    """(label, argv) of every run of the sweep, in order."""
+    """(label, argv) of every run of the sweep, in order; a multi-rank argv
+    holds PORT_ARG, which launch_argv fills in."""
     common = ["--frags-per-rank", str(k["F"]), "--samples", str(k["SAMPLES"]), "--warmups", str(k["WARMUPS"]),
               "--repeats", str(k["R"]), "--csv", k["OUT_CSV"]]
     out = []
@@ -57,11 +62,16 @@ def commands(k, extra=()):
             args += common + list(extra)
             if k["NP"] > 1:
                 argv = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={k['NP']}",
-                        "--master-addr=127.0.0.1", f"--master-port={free_port()}", "--no-python", DRIVER] + args
+                        "--master-addr=127.0.0.1", PORT_ARG, "--no-python", DRIVER] + args
             else:
                 argv = [DRIVER] + args
             out.append((f"S = {size}, {label}", argv))
     return out
+
+
+def launch_argv(argv):
+    """argv with a free loopback port in place of PORT_ARG, chosen now."""
+    return [a.format(port=free_port()) if a == PORT_ARG else a for a in argv]
 
 
 def main(argv=None):
@@ -80,7 +90,7 @@ def main(argv=None):
     for label, cmd in runs:
         print(f"--- {label}: {shlex.join(cmd)}", flush=True)
         if not dry:
-            r = subprocess.run(cmd)
+            r = subprocess.run(launch_argv(cmd))
             if r.returncode != 0:
                 sys.exit(f"run failed ({r.returncode}): {label}")
     print(f"CSV: {os.path.abspath(k['OUT_CSV'])} (baseline_gflops_mean / protected_gflops_mean per row; "

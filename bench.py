@@ -1,25 +1,38 @@
 #!/usr/bin/env python
 """Protected SGEMM throughput and ABFT overhead vs unprotected cuBLAS SGEMM.
 
-Workload (per rank, weak scaling): a 4096 x 4096 C tile with K = 4096 on a
-Pr x Pc grid (global M = Pr*4096, N = Pc*4096), FP32 A and B i.i.d.
-uniform[-1,1] (mt19937_64, seeds 123456 / 987654), F = 4 column fragments,
-double-buffered C, one SWIFI single-bit flip (bit uniform over 0-31) per
-iteration, detection threshold 1e-5*K*max|A|*max|B|. One step = one trial of
-20 protected iterations (the reference's --repeats sample). A and B panels are
-broadcast from rank 0 over NCCL before timing.
+Default workload (global16384): global M = N = K = 16384 FP32 with strong
+scaling. The N GPUs form choose_grid's near-square Pr x Pc grid (1x1, 1x2,
+2x2, 2x4 at N = 1, 2, 4, 8) and each rank owns one output tile (16384x16384,
+16384x8192, 8192x8192, 8192x4096) with its full K. A and B are i.i.d.
+uniform[-1,1] (mt19937_64, seeds 123456 / 987654), F = 4 column fragments
+per tile, double-buffered C, one SWIFI single-bit flip (bit uniform over
+0-31) per rank per iteration, detection threshold 1e-5*K*max|A|*max|B|.
+One step = one protected iteration of every rank's tile: the F fragment
+SGEMMs, each fragment's verification, and localisation + correction after a
+detection. Step j carries the injection of iteration j of one trial (seed
+base + rank*7919 + j*104729), so a 20-step run is the workload's 20
+iterations. The A and B panels are broadcast from rank 0 over NCCL before
+timing; nothing crosses NVLink inside the timed loop.
+
+--workload tile4096: a 4096 x 4096 tile with K = 4096 per rank (weak
+scaling), 20 protected iterations per step (one trial of the reference's
+--repeats 20 per step, trial seeds base + t*31337).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--verify-kernel auto|ldg|tma] [--timeline TRACE_JSON]
-    python bench.py --verify-sweep [--verify-kernel auto|ldg|tma]
+                    [--workload global16384|tile4096] [--verify-kernel auto|ldg|tma]
+                    [--timeline TRACE_JSON]
+    python bench.py --verify-sweep [--verify-kernel auto|ldg|tma] [--sweep-shapes MxNxLDC,...]
+                    [--sweep-launches L] [--sweep-warmup W]
 
 Rank 0 prints one JSON line. `value` is whole-job protected TFLOP/s
-(2*M*N*K*iterations / max-over-ranks device time); `e2e` the same through
-host buffers (copies timed); `roofline` the verify kernel against the
+(2*M*N*K per iteration over the max-over-ranks device time of each step);
+`e2e` the same through host buffers (the copies of every step's A, B and C
+timed); `roofline` the verify kernel on this grid's fragment shape against the
 measured HBM copy bandwidth; `cpu_baseline` the protected iterations on the
-host cores. `--impl reference` times the reference's algorithm on the host
-cores (CPU oracle + BLAS SGEMM). `--timeline` adds a CUPTI kernel timeline
-of one protected trial and the ABFT kernels' overlap with the SGEMMs.
+host cores, with the ABFT-only host time beside it. `--impl reference` times
+the reference's algorithm on the host cores (CPU oracle + BLAS SGEMM), and
+imports nothing of the product package.
 """
 import argparse
 import importlib
@@ -35,6 +48,12 @@ sys.path.insert(0, ROOT)
 PKG = "asynchronous_abft_for_mpi-cuda_architectures_b200"
 METRIC = "protected SGEMM TFLOPS and ABFT overhead % vs unprotected"
 FALLBACK_HBM_GBS = 6650.0
+INJECT_IT_STRIDE = 104729  # per-iteration step of the injection seed (pipeline/passes.cuh:149-151)
+TRIAL_SEED_STRIDE = 31337  # per-trial step of the base seed (main.cu:243-244)
+WORKLOADS = {
+    "global16384": {"kind": "global", "size": 16384, "iters": 1},
+    "tile4096": {"kind": "tile", "size": 4096, "iters": 20},
+}
 
 
 def parse():
@@ -43,43 +62,95 @@ def parse():
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--tile", type=int, default=4096, help="per-rank C tile edge (M_b = N_b)")
-    p.add_argument("--K", type=int, default=4096)
+    p.add_argument("--workload", choices=sorted(WORKLOADS), default="global16384")
+    p.add_argument("--size", type=int, default=None,
+                   help="global16384: global M = N = K; tile4096: per-rank tile edge and K")
     p.add_argument("--frags", type=int, default=4)
-    p.add_argument("--iters", type=int, default=20, help="protected iterations per step")
+    p.add_argument("--iters", type=int, default=None, help="protected iterations per step (workload default)")
     p.add_argument("--mode", choices=["none", "add", "swifi"], default="swifi")
     p.add_argument("--zone", default="any")
     p.add_argument("--seed-a", type=int, default=123456)
     p.add_argument("--seed-b", type=int, default=987654)
     p.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU-baseline work")
+    p.add_argument("--ref-rows", type=int, default=2048,
+                   help="reference arm: rows of the rank tile in each step's host sample")
     p.add_argument("--no-e2e", action="store_true")
-    p.add_argument("--no-graph", action="store_true", help="enqueue the loop from the host every trial")
+    p.add_argument("--no-graph", action="store_true", help="enqueue the loop from the host every step")
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--verify-kernel", choices=["auto", "ldg", "tma"], default="auto",
                    help="verify body: by fragment size, 128-bit loads, or TMA-staged")
     p.add_argument("--verify-sweep", action="store_true",
                    help="instead of the benchmark: the verify kernel alone on the fragment shapes of the "
                         "workloads (L2 emptied before each launch, mean of 30 launches), one JSON line per shape")
+    p.add_argument("--sweep-shapes", default=None, metavar="MxNxLDC,...",
+                   help="--verify-sweep: these fragment shapes (rows x columns x row pitch) instead of the workloads'")
+    p.add_argument("--sweep-launches", type=int, default=30, help="--verify-sweep: timed launches per shape")
+    p.add_argument("--sweep-warmup", type=int, default=3, help="--verify-sweep: untimed launches per shape")
     p.add_argument("--timeline", default=None, metavar="TRACE_JSON",
-                   help="after the timed runs, record one protected trial with the CUDA profiler (CUPTI "
+                   help="after the timed runs, record one protected step with the CUDA profiler (CUPTI "
                         "kernel records, cuBLAS included) into this Chrome trace and report how much of "
                         "the ABFT kernels' time overlapped an SGEMM")
-    return p.parse_args()
+    a = p.parse_args()
+    w = WORKLOADS[a.workload]
+    a.kind = w["kind"]
+    a.size = a.size or w["size"]
+    a.iters = a.iters or w["iters"]
+    return a
 
 
-def workload(args, Pr, Pc):
+class Geometry:
+    """Global problem and one rank's tile (main.cu:32-69), from the helpers of
+    `h` (the product's host module, or the oracle for the CPU arm: same names,
+    same results)."""
+
+    def __init__(self, args, world, rank, h):
+        self.Pr, self.Pc = h.choose_grid(world)
+        if args.kind == "global":
+            self.M = self.N = self.K = args.size
+        else:
+            self.M, self.N, self.K = self.Pr * args.size, self.Pc * args.size, args.size
+        pr, pc = rank // self.Pc, rank % self.Pc
+        rc, ro = h.split_dim(self.M, self.Pr)
+        cc, co = h.split_dim(self.N, self.Pc)
+        self.M_b, self.N_b = int(rc[pr]), int(cc[pc])
+        self.row_off, self.col_off = int(ro[pr]), int(co[pc])
+        self.F = h.frag_count(self.M, self.K, self.N, self.M_b, self.N_b, args.frags)
+        self.counts, self.offsets = h.split_dim(self.N_b, self.F)
+
+
+def workload(args, g):
+    if args.kind == "global":
+        name = (f"protected SGEMM global {g.M}x{g.N}x{g.K} (strong scaling) on a {g.Pr}x{g.Pc} grid, "
+                f"{g.M_b}x{g.N_b} tile per rank, F={g.F}, double-buffered C, {args.mode} faults (zone {args.zone}), "
+                f"tau=1e-5*K*max|A|*max|B|, {args.iters} iteration(s) per step")
+    else:
+        name = (f"protected SGEMM {g.M_b}x{g.N_b}x{g.K} per rank on a {g.Pr}x{g.Pc} grid (global "
+                f"{g.M}x{g.N}x{g.K}, weak scaling), F={g.F}, double-buffered C, {args.mode} faults "
+                f"(zone {args.zone}), tau=1e-5*K*max|A|*max|B|, {args.iters} iterations per step")
+    per_rank = 4 * (g.M_b * g.K + g.K * g.N_b + 2 * g.M_b * g.N_b)
     return {
-        "workload": f"protected SGEMM {args.tile}x{args.tile}x{args.K} per rank on a {Pr}x{Pc} grid "
-                    f"(global {Pr * args.tile}x{Pc * args.tile}x{args.K}), F={args.frags}, double-buffered C, "
-                    f"{args.mode} faults (zone {args.zone}), tau=1e-5*K*max|A|*max|B|",
-        "M": Pr * args.tile, "N": Pc * args.tile, "K": args.K, "tile": [args.tile, args.tile],
-        "grid": [Pr, Pc], "frags_per_rank": args.frags, "iters_per_step": args.iters,
+        "workload": name, "name": args.workload,
+        "M": g.M, "N": g.N, "K": g.K, "tile": [g.M_b, g.N_b], "grid": [g.Pr, g.Pc],
+        "frags_per_rank": g.F, "fragment": [g.M_b, int(max(g.counts))], "iters_per_step": args.iters,
         "inject": args.mode, "swifi_zone": args.zone,
-        "l2": "inputs larger than L2 (A, B, 2 x C per rank = 256 MiB > 126 MB)",
-        "parallelism": f"{Pr}x{Pc} output-tile grid, one rank per GPU",
-        "loop": "host-enqueued" if args.no_graph else "CUDA graph per trial",
+        "l2": f"inputs larger than L2 (A, B, 2 x C per rank = {per_rank / 2**20:.0f} MiB > 126 MB)",
+        "parallelism": f"{g.Pr}x{g.Pc} output-tile grid, one rank per GPU",
+        "loop": "host-enqueued" if args.no_graph else "CUDA graph per step",
         "verify_kernel": args.verify_kernel,
     }
+
+
+def step_seed(args, base, j):
+    """Base seed of step j (warm-up steps first, then the timed ones)."""
+    if args.iters == 1:
+        return base + j * INJECT_IT_STRIDE
+    return base + j * TRIAL_SEED_STRIDE
+
+
+def relative_threshold(A, B, K, rel=1e-5):
+    """The workloads' detection threshold rel * K * max|A| * max|B|."""
+    import numpy as np
+    return float(rel) * float(K) * float(np.abs(A).max()) * float(np.abs(B).max())
 
 
 def peak_hbm():
@@ -90,17 +161,27 @@ def peak_hbm():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def verify_traffic_per_launch(tile, frags, kernel):
-    """DRAM bytes per verify launch from the committed ncu summary of this fragment
-    shape and verify body, if any (fragments below 512 MiB run the 128-bit-load
-    body unless the TMA one is forced)."""
+def verify_traffic_per_launch(M_b, N_f, kernel):
+    """DRAM bytes per verify launch from the committed ncu summary of this
+    fragment shape and verify body, if any."""
     body = "verify_tma" if kernel == "tma" else "verify"
-    path = os.path.join(ROOT, "profiles", f"{body}_{tile}x{tile // frags}.md")
+    path = os.path.join(ROOT, "profiles", f"{body}_{M_b}x{N_f}.md")
     try:
         with open(path) as f:
             for line in f:
                 if line.startswith("traffic_bytes_per_launch:"):
                     return float(line.split(":")[1])
+    except OSError:
+        pass
+    return None
+
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
     except OSError:
         pass
     return None
@@ -164,51 +245,48 @@ class ClockSampler:
                 "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
-def cpu_baseline(abft, A, B, counts, offsets, tau, args, budget_s, iters_cap):
-    from oracle import cpu_baseline as cb
-    r = cb.protected_iterations(A, B, counts, offsets, tau, args.mode, args.zone, args.seed_a + args.seed_b, 0,
-                                iters_cap, golden=None, time_budget_s=budget_s)
-    return r, cb.host_threads()
-
-
 def run_reference(args):
-    """CPU arm: the reference's algorithm on the host cores (rank 0 only)."""
+    """CPU arm (rank 0 only): the reference's algorithm on the host cores. It
+    imports the oracle only, never the product package."""
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
     if rank != 0:
         return
-    abft = importlib.import_module(PKG)
     import numpy as np
     from oracle import cpu_baseline as cb
     from oracle import oracle as orc
-    Pr, Pc = abft.choose_grid(max(world, args.gpus))
-    M_b = N_b = args.tile
-    K = args.K
-    A = orc.fill_random(M_b * K, args.seed_a).reshape(M_b, K)
-    B = orc.fill_random(K * N_b, args.seed_b).reshape(K, N_b)
-    counts, offsets = orc.split_dim(N_b, args.frags)
-    tau = np.full(args.frags, abft.relative_threshold(A, B, K))
+    g = Geometry(args, max(world, args.gpus), 0, orc)
+    A_full = orc.fill_random(g.M * g.K, args.seed_a).reshape(g.M, g.K)
+    B_full = orc.fill_random(g.K * g.N, args.seed_b).reshape(g.K, g.N)
+    tau = relative_threshold(A_full, B_full, g.K)
+    rows = min(g.M_b, args.ref_rows)
+    A = np.ascontiguousarray(A_full[:rows])
+    B = np.ascontiguousarray(B_full[:, :g.N_b])
+    del A_full, B_full
+    taus = np.full(g.F, tau)
+    base = args.seed_a + args.seed_b
     for w in range(args.warmup):
-        cb.protected_iterations(A, B, counts, offsets, tau, args.mode, args.zone, args.seed_a + args.seed_b, 0, 1)
+        cb.protected_iterations(A, B, g.counts, g.offsets, taus, args.mode, args.zone, step_seed(args, base, w), 0, 1)
     secs = flops = 0.0
     per_step = []
     for t in range(args.steps):
-        r = cb.protected_iterations(A, B, counts, offsets, tau, args.mode, args.zone,
-                                    args.seed_a + args.seed_b + t * 31337, 0, 1)
+        r = cb.protected_iterations(A, B, g.counts, g.offsets, taus, args.mode, args.zone,
+                                    step_seed(args, base, args.warmup + t), 0, 1)
         secs += r["seconds"]
         flops += r["flops"]
         per_step.append(r["seconds"] * 1e3)
-    # the grid's ranks are independent tiles: the whole job on one host runs them one after another
     value = flops / secs / 1e12
     cores = cb.host_threads()
-    sample = (f"1 protected iteration of one {M_b}x{N_b}x{K} rank tile per step (numpy SGEMM + oracle "
-              f"verification/localisation/correction), {args.steps} steps")
+    sample = (f"each step: 1 protected iteration of rows 0..{rows - 1} of rank 0's {g.M_b}x{g.N_b} tile "
+              f"(a {rows}x{g.N_b}x{g.K} protected SGEMM: numpy SGEMM + oracle verification, localisation and "
+              f"correction), {args.steps} steps")
     line = {
         "metric": METRIC, "impl": "reference", "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": statistics.median(per_step),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (f64 checksums)",
-        "data": "synthetic uniform[-1,1] (mt19937_64)", "config": workload(args, Pr, Pc),
-        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample},
+        "higher_is_better": True, "scaling": "strong" if args.kind == "global" else "weak", "vs_baseline": None,
+        "dtype": "f32 (f64 checksums)", "data": "synthetic uniform[-1,1] (mt19937_64)", "config": workload(args, g),
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample,
+                         "cpu_model": cpu_model(), "nproc": os.cpu_count()},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -285,28 +363,6 @@ def isolated_localize_ms(abft, torch, s, reps=16):
     return statistics.mean(times)
 
 
-def isolated_verify_large(abft, torch, device, M=16384, N=4096, reps=9):
-    """The same verify kernel alone on one large fragment (M x N floats), L2
-    emptied before each launch: (bytes per launch, mean ms)."""
-    C = torch.randn((M, N), dtype=torch.float32, device=device)
-    ws = abft.kernels.Workspace(M, N, 1, [N], [0])
-    st = torch.cuda.Stream(device=device)
-    cold = ColdL2(torch, device)
-    times = []
-    with torch.cuda.stream(st):
-        for _ in range(reps):
-            cold()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(st)
-            abft.host.call("abft_verify", ws.handle, C.data_ptr(), C.stride(0), 0, 1e30, 0, -1, st.cuda_stream)
-            e1.record(st)
-            e1.synchronize()
-            times.append(e0.elapsed_time(e1))
-    ws.close()
-    del C, cold
-    return 4.0 * M * N + 24.0 * N, statistics.mean(times)
-
-
 def overlap_timeline(torch, s, args, base, rank, path):
     """One protected trial under torch.profiler: every kernel's device start and
     end (CUPTI), written as a Chrome trace. Reports, per ABFT kernel, the share
@@ -354,39 +410,63 @@ def overlap_timeline(torch, s, args, base, rank, path):
     }
 
 
+def cpu_baseline(A, B, C_clean, g, tau, args, base):
+    """Rank 0 at N = 1: the protected iterations on the host cores (numpy SGEMM
+    + the oracle's verification), and the ABFT work alone on the GPU's own C."""
+    import numpy as np
+    from oracle import cpu_baseline as cb
+    taus = np.full(g.F, tau)
+    r = cb.protected_iterations(A, B, g.counts, g.offsets, taus, args.mode, args.zone, step_seed(args, base, 0), 0,
+                                args.iters * max(args.steps, 1), time_budget_s=args.cpu_budget)
+    ab = cb.abft_only(C_clean, A, B, g.counts, g.offsets, taus, args.mode, args.zone, step_seed(args, base, 0), 0,
+                      time_budget_s=max(2.0, args.cpu_budget / 2))
+    cores = cb.host_threads()
+    return {
+        "value": r["flops"] / r["seconds"] / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+        "sample": f"{r['iters']} protected iteration(s) of the {g.M_b}x{g.N_b}x{g.K} tile (numpy SGEMM + oracle "
+                  f"verification/localisation/correction), {r['seconds']:.1f} s",
+        "abft_only_ms": ab["verify_ms"], "abft_encode_ms": ab["encode_ms"],
+        "abft_only": f"the oracle's verification of one iteration on the GPU's own fault-free C with that "
+                     f"iteration's planted fault (actualRow + detect on all {g.F} fragments, then the reference's "
+                     f"on-demand localisation and correction), mean of {ab['reps']}; encode (colSumA, expectedRow) "
+                     f"timed apart; {cores} host threads",
+        "cpu_model": cpu_model(), "nproc": os.cpu_count(),
+    }
+
+
 def run_ours(args):
     import numpy as np
     import torch
 
     abft = importlib.import_module(PKG)
     abft.set_verify_kernel(args.verify_kernel)
-    from importlib import import_module
-    dist_mod = import_module(f"{PKG}.distributed")
+    dist_mod = importlib.import_module(f"{PKG}.distributed")
     rank, world, local = dist_mod.init_from_env(timeout_s=300)
     if world != args.gpus and not (world == 1 and args.gpus == 1):
         args.gpus = world
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     grid = dist_mod.Grid2D(world, rank)
-    Pr, Pc = grid.Pr, grid.Pc
-    M, N, K = Pr * args.tile, Pc * args.tile, args.K
+    g = Geometry(args, world, rank, abft.host)
+    assert (g.Pr, g.Pc) == (grid.Pr, grid.Pc)
+    M, N, K = g.M, g.N, g.K
 
     A_full = B_full = None
     tau0 = 0.0
     if rank == 0:
         A_h = abft.fill_random(M * K, args.seed_a).reshape(M, K)
         B_h = abft.fill_random(K * N, args.seed_b).reshape(K, N)
-        tau0 = abft.relative_threshold(A_h, B_h, K)
+        tau0 = relative_threshold(A_h, B_h, K)
         A_full = torch.from_numpy(A_h).to(dev)
         B_full = torch.from_numpy(B_h).to(dev)
         del A_h, B_h
     A, B = dist_mod.distribute_panels(grid, M, K, N, A_full, B_full, dev)
     del A_full, B_full
     torch.cuda.synchronize(dev)
+    torch.cuda.empty_cache()
     tau = dist_mod.allreduce([tau0], "sum", dev)[0]
-    t = abft.rank_tile(M, K, N, Pr, Pc, rank, args.frags)
-    s = abft.OnlineSession(A, B, counts=t.counts, offsets=t.offsets, max_iters=args.iters)
-    s.set_tau([tau] * t.F)
+    s = abft.OnlineSession(A, B, counts=g.counts, offsets=g.offsets, max_iters=max(args.iters, 1))
+    s.set_tau([tau] * g.F)
     s.encode()  # first call loads the kernels
     encode_ms = s.encode()
     s.baseline(1)
@@ -395,11 +475,16 @@ def run_ours(args):
     if args.mode == "swifi":
         s.set_golden(golden)  # the reference captures the fault-free C only for SWIFI runs
     base = args.seed_a + args.seed_b
+    graph = not args.no_graph
+
+    def protected(j):
+        return s.online(args.mode, args.zone, base_seed=step_seed(args, base, j), rank=rank, repeats=args.iters,
+                        graph=graph)
 
     for w in range(args.warmup):
-        s.baseline(args.iters, graph=not args.no_graph)
-        s.online(args.mode, args.zone, base_seed=base + w * 31337, rank=rank, repeats=args.iters,
-                 graph=not args.no_graph)
+        s.baseline(args.iters, graph=graph)
+        s.baseline_monolithic(args.iters, graph=graph)
+        protected(w)
 
     def region(fn, calls=None):
         dist_mod.barrier(dev)
@@ -409,34 +494,34 @@ def run_ours(args):
         dist_mod.barrier(dev)
         return out
 
-    b_ms = region(lambda i: s.baseline(args.iters, graph=not args.no_graph)[0])
+    b_ms = region(lambda i: s.baseline(args.iters, graph=graph)[0])
+    m_ms = region(lambda i: s.baseline_monolithic(args.iters, graph=graph)[0])
     sampler = ClockSampler(torch, dev)
     sampler.start()
-    p_res = region(lambda i: s.online(args.mode, args.zone, base_seed=base + (args.warmup + i) * 31337, rank=rank,
-                                      repeats=args.iters, graph=not args.no_graph))
+    p_res = region(lambda i: protected(args.warmup + i))
     clocks = sampler.stop()
     p_ms = [r["device_ms"] for r in p_res]
     cm = np.sum([r["cm"] for r in p_res], axis=0).tolist()
     restored = int(sum(r["n_restored"] for r in p_res))
     launches = int(sum(r["kernel_launches"] for r in p_res))
 
-    # live per-launch verify timing (same loop, CUDA events around each verify on the verify stream)
-    prof = s.online(args.mode, args.zone, base_seed=base, rank=rank, repeats=args.iters, profile=True)
+    # live per-launch verify timing (one step, CUDA events around each verify on the verify stream)
+    prof = s.online(args.mode, args.zone, base_seed=step_seed(args, base, 0), rank=rank, repeats=args.iters,
+                    profile=True)
     iso_ms = isolated_verify_ms(abft, torch, s)
     loc_ms = isolated_localize_ms(abft, torch, s)
-    large_bytes, large_ms = isolated_verify_large(abft, torch, dev)
 
     e2e_ms = []
     e2e_single_ms = []
-    h2d = 4 * (t.M_b * K + K * t.N_b)
-    d2h = 4 * t.M_b * t.N_b + 20
+    h2d = 4 * (g.M_b * K + K * g.N_b)
+    d2h = 4 * g.M_b * g.N_b + 20
     if not args.no_e2e:
         hA = A.cpu().pin_memory()
         hB = B.cpu().pin_memory()
-        hC = torch.empty((t.M_b, t.N_b), dtype=torch.float32).pin_memory()
-        seeds = [base + i * 31337 for i in range(args.steps)]
-        # one call per step: its inputs in, encode, loop, result out, then the next call
-        s.run_host(hA, hB, hC, args.mode, args.zone, base_seed=base, rank=rank, repeats=args.iters)
+        hC = torch.empty((g.M_b, g.N_b), dtype=torch.float32).pin_memory()
+        seeds = [step_seed(args, base, args.warmup + i) for i in range(args.steps)]
+        # one call per step: its inputs in, encode, the step's iterations, its result out, then the next call
+        s.run_host(hA, hB, hC, args.mode, args.zone, base_seed=seeds[0], rank=rank, repeats=args.iters)
         single = region(lambda i: s.run_host(hA, hB, hC, args.mode, args.zone, base_seed=seeds[i], rank=rank,
                                              repeats=args.iters))
         e2e_single_ms = [r["e2e_ms"] for r in single]
@@ -448,9 +533,11 @@ def run_ours(args):
         whole = region(lambda i: s.run_host_steps([hA] * n, [hB] * n, [hC] * n, seeds, args.mode, args.zone,
                                                   rank=rank, repeats=args.iters), calls=1)
         e2e_ms = [whole[0][1] / n] * n
+        del hA, hB, hC
 
     # max over ranks, per step
     b_max = dist_mod.allreduce(b_ms, "max", dev)
+    m_max = dist_mod.allreduce(m_ms, "max", dev)
     p_max = dist_mod.allreduce(p_ms, "max", dev)
     e_max = dist_mod.allreduce(e2e_ms, "max", dev) if e2e_ms else []
     e1_max = dist_mod.allreduce(e2e_single_ms, "max", dev) if e2e_single_ms else []
@@ -460,63 +547,63 @@ def run_ours(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        r, cores = cpu_baseline(abft, A.cpu().numpy(), B.cpu().numpy(), t.counts, t.offsets,
-                                np.full(t.F, tau), args, args.cpu_budget, args.iters)
-        cpu = {"value": r["flops"] / r["seconds"] / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "port",
-               "sample": f"{r['iters']} protected iteration(s) of the {t.M_b}x{t.N_b}x{K} tile "
-                         f"(numpy SGEMM + oracle verification/localisation/correction), {r['seconds']:.1f} s"}
+        cpu = cpu_baseline(A.cpu().numpy(), B.cpu().numpy(), golden.cpu().numpy(), g, tau, args, base)
 
-    tl = overlap_timeline(torch, s, args, base, rank, args.timeline) if (args.timeline and rank == 0) else None
+    tl = overlap_timeline(torch, s, args, step_seed(args, base, 0), rank, args.timeline) \
+        if (args.timeline and rank == 0) else None
     s.close()
     if rank == 0:
         flops_step = 2.0 * M * N * K * args.iters
         total_p = sum(p_max)
         value = flops_step * args.steps / (total_p * 1e-3) / 1e12
         base_tf = flops_step * args.steps / (sum(b_max) * 1e-3) / 1e12
-        med_b, med_p = statistics.median(b_max), statistics.median(p_max)
-        N_f = int(max(t.counts))
-        bytes_launch = 4.0 * t.M_b * N_f + 24.0 * N_f
+        mono_tf = flops_step * args.steps / (sum(m_max) * 1e-3) / 1e12
+        med_b, med_m, med_p = statistics.median(b_max), statistics.median(m_max), statistics.median(p_max)
+        N_f = int(max(g.counts))
+        bytes_launch = 4.0 * g.M_b * N_f + 24.0 * N_f
         peak, peak_kind = peak_hbm()
         live_gbs = bytes_launch / (v_avg_max[0] * 1e-3) / 1e9 if v_avg_max[0] > 0 else None
         iso_gbs = bytes_launch / (v_avg_max[1] * 1e-3) / 1e9 if v_avg_max[1] > 0 else None
-        large_gbs = large_bytes / (large_ms * 1e-3) / 1e9 if large_ms > 0 else None
-        loc_bytes = 4.0 * t.M_b * N_f + 24.0 * t.M_b
+        loc_bytes = 4.0 * g.M_b * N_f + 24.0 * g.M_b
         loc_gbs = loc_bytes / (v_avg_max[2] * 1e-3) / 1e9 if v_avg_max[2] > 0 else None
-        traffic = verify_traffic_per_launch(args.tile, args.frags, args.verify_kernel)
+        traffic = verify_traffic_per_launch(g.M_b, N_f, args.verify_kernel)
         line = {
             "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": total_p / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32 (f64 checksums)",
+            "scaling": "strong" if args.kind == "global" else "weak", "vs_baseline": None,
+            "dtype": "f32 (f64 checksums)",
             "data": "synthetic uniform[-1,1] (mt19937_64, seeds 123456/987654)",
-            "config": workload(args, Pr, Pc),
-            "overhead_pct": (med_p / med_b - 1.0) * 100.0,
-            "overhead_pct_total": (total_p / sum(b_max) - 1.0) * 100.0,
+            "config": workload(args, g),
+            "overhead_pct": (total_p / sum(b_max) - 1.0) * 100.0,
+            "overhead_pct_median": (med_p / med_b - 1.0) * 100.0,
+            "overhead_vs_monolithic_pct": (total_p / sum(m_max) - 1.0) * 100.0,
             "baseline_tflops": base_tf,
             "baseline_kind": "unprotected cuBLAS SGEMM, same F fragments (pass_baseline)"
-                             + ("" if args.no_graph else ", CUDA graph per trial"),
+                             + ("" if args.no_graph else ", CUDA graph per step"),
+            "baseline_monolithic_tflops": mono_tf,
+            "baseline_monolithic_kind": "unprotected cuBLAS SGEMM, one call on the whole tile per iteration",
             "encode_ms": encode_ms,
             "confusion_matrix": {"TP": int(cm_all[0]), "TN": int(cm_all[1]), "FP": int(cm_all[2]),
                                  "FN": int(cm_all[3]), "restored": int(cm_all[4])},
             "roofline": {
-                "kernel": f"fused verify (actualRow + detect), one {t.M_b}x{N_f} fragment per launch",
+                "kernel": f"fused verify (actualRow + detect), one {g.M_b}x{N_f} fragment (row pitch {g.N_b}) "
+                          "per launch",
                 "bound": "hbm", "achieved": iso_gbs, "peak": peak, "unit": "GB/s",
                 "frac": (iso_gbs / peak) if iso_gbs else None, "traffic": traffic,
                 "peak_kind": f"{peak_kind} hbm_gbs (copy burst; the kernel is timed alone)",
                 "bytes_per_launch": bytes_launch, "launch_ms": v_avg_max[1],
-                "timing": "CUDA events on the launching stream around each launch, kernel alone, "
-                          "L2 emptied before each launch (256 MiB written, then 256 MiB read so no dirty "
-                          "lines are written back during the launch), mean of 24 launches (event timestamps "
-                          "advance in ~2 us steps; the mean of many intervals is unbiased, their median is not)",
+                "timing": "CUDA events on the launching stream around each launch, kernel alone on the session's "
+                          "own C buffers, L2 emptied before each launch (256 MiB written, then 256 MiB read so no "
+                          "dirty lines are written back during the launch), mean of 6 launches per fragment and "
+                          "buffer, max over ranks",
                 "live": {"achieved": live_gbs, "frac": (live_gbs / peak) if live_gbs else None,
                          "launch_ms": v_avg_max[0],
-                         "note": "inside the protected loop on the low-priority verify stream: the kernel "
-                                 "waits for SMs the SGEMM releases, so its wall time is not a bandwidth measure"},
-                "localize": {"kernel": f"gated localise + correct, full pass over one {t.M_b}x{N_f} fragment "
+                         "note": "inside a protected step on the low-priority verify stream: the kernel waits for "
+                                 "SMs the SGEMM releases, so its wall time is not a bandwidth measure"},
+                "localize": {"kernel": f"gated localise + correct, full pass over one {g.M_b}x{N_f} fragment "
                                        "with a planted fault (row sums, row arg-max, correction)",
                              "achieved": loc_gbs, "frac": (loc_gbs / peak) if loc_gbs else None,
                              "launch_ms": v_avg_max[2], "bytes_per_launch": loc_bytes},
-                "large_fragment": {"shape": [16384, 4096], "achieved": large_gbs,
-                                   "frac": (large_gbs / peak) if large_gbs else None, "launch_ms": large_ms},
             },
             "gpu_launches": int(cm_all[5]),
             "clocks": clocks,
@@ -526,8 +613,9 @@ def run_ours(args):
                            "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
                            "ms_per_step": sum(e_max) / len(e_max),
                            "path": "OnlineSession.run_host_steps -> abft_session_run_host_steps: every step "
-                                   "copies its A and B in from pinned host memory and its final C and counters "
-                                   "out; step k+1's inputs are copied while step k computes",
+                                   "copies its A and B in from pinned host memory, encodes, runs its protected "
+                                   "iteration(s) and copies its final C and counters out; step k+1's inputs "
+                                   "are copied while step k computes",
                            "one_call_per_step": {
                                "value": flops_step * len(e1_max) / (sum(e1_max) * 1e-3) / 1e12,
                                "ms_per_step": sum(e1_max) / len(e1_max),
@@ -541,17 +629,20 @@ def run_ours(args):
 
 
 # Fragment shapes (rows M_b, columns N_f, row pitch) of the workloads: F = 4
-# fragments of the rank tile, from 1024^3 to 16384^3 on one GPU, the 2x4
-# grid's tiles, the non-square shapes, and a 1 GiB fragment.
-SWEEP_SHAPES = [(1024, 256, 1024), (4096, 512, 2048), (4096, 1024, 4096), (16384, 256, 1024),
-                (1024, 4096, 16384), (8192, 1024, 4096), (8192, 2048, 8192), (16384, 2048, 8192),
-                (16384, 4096, 16384), (65536, 4096, 4096)]
+# fragments of the rank tile: 1024^3 and 4096^3 on one GPU, the 16384^3
+# tiles at 1, 2, 4 and 8 GPUs, the 8192^3 2x4 tile, the non-square shapes,
+# and a 1 GiB fragment.
+SWEEP_SHAPES = [(1024, 256, 1024), (4096, 1024, 4096), (16384, 4096, 16384), (16384, 2048, 8192),
+                (8192, 2048, 8192), (8192, 1024, 4096), (4096, 512, 2048), (16384, 256, 1024),
+                (1024, 4096, 16384), (65536, 4096, 4096)]
 
 
 def verify_sweep(args):
     """The verify kernel alone per fragment shape (body selected by
     --verify-kernel): L2 emptied before each launch, CUDA events on the
-    launching stream, mean of 30 launches after 3 untimed ones."""
+    launching stream, mean of --sweep-launches launches after --sweep-warmup
+    untimed ones. The verify launches of shape i are launches
+    i * (warmup + launches) ... of the process (ncu -k regex:k_verify -s/-c)."""
     import torch
     abft = importlib.import_module(PKG)
     dev = torch.device("cuda", 0)
@@ -560,19 +651,22 @@ def verify_sweep(args):
     peak, peak_kind = peak_hbm()
     cold = ColdL2(torch, dev)
     st = torch.cuda.Stream(device=dev)
-    for M, N, ldc in SWEEP_SHAPES:
+    shapes = SWEEP_SHAPES
+    if args.sweep_shapes:
+        shapes = [tuple(int(x) for x in sh.split("x")) for sh in args.sweep_shapes.split(",")]
+    for M, N, ldc in shapes:
         C = torch.randn((M, ldc), dtype=torch.float32, device=dev)
         ws = abft.kernels.Workspace(M, ldc, 64, [N], [0])
         times = []
         with torch.cuda.stream(st):
-            for k in range(33):
+            for k in range(args.sweep_warmup + args.sweep_launches):
                 cold()
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record(st)
                 abft.host.call("abft_verify", ws.handle, C.data_ptr(), ldc, 0, 1e30, 0, -1, st.cuda_stream)
                 e1.record(st)
                 e1.synchronize()
-                if k >= 3:
+                if k >= args.sweep_warmup:
                     times.append(e0.elapsed_time(e1) * 1e3)
         ws.close()
         del C

@@ -291,6 +291,11 @@ int abft_session_encode(abft_session* s, double* encode_ms);
  * graph = 1 replays them as a CUDA graph (captured once per repeats), the
  * unprotected counterpart of abft_online_args.graph. */
 int abft_session_baseline(abft_session* s, int repeats, int graph, double* device_ms, double* host_ms);
+/* A stricter unprotected baseline with no counterpart in the reference:
+ * repeats x ONE SGEMM of the whole M_b x N_b tile (gemm_cublas,
+ * kernels/gemm_cublas.cuh:7-22, called once instead of F times), so that the
+ * cost of splitting C into fragments shows apart from the ABFT kernels. */
+int abft_session_baseline_monolithic(abft_session* s, int repeats, int graph, double* device_ms, double* host_ms);
 /* pass_online_loop, pipeline/passes.cuh:90-227 (timed part). */
 int abft_session_online(abft_session* s, const abft_online_args* args, abft_online_result* res);
 /* Injection log of the last online call: it_count x {frag, row, col, bit}

@@ -24,6 +24,23 @@ def host_threads():
         return os.cpu_count() or 1
 
 
+def inject(C, seed, counts, offsets, mode, lo, hi):
+    """The reference's fault of one iteration (pipeline/passes.cuh:149-170,
+    kernels/swifi.cuh:61-114) applied to C in place; returns the fragment (-1:
+    none)."""
+    if mode not in ("add", "swifi"):
+        return -1
+    frag = orc.inject_frag(seed, len(counts))
+    Cf = C[:, offsets[frag]:]
+    if mode == "add":
+        r, c, _ = orc.inject_position(seed, frag, C.shape[0], counts[frag])
+        Cf[r, c] = np.float32(Cf[r, c] + np.float32(1.0e6))
+    else:
+        r, c, b = orc.inject_position(seed, frag, C.shape[0], counts[frag], lo, hi)
+        Cf.view(np.uint32)[r, c] ^= np.uint32(1 << b)
+    return frag
+
+
 def protected_iterations(A, B, counts, offsets, tau, mode, zone, base_seed, rank, iters, golden=None,
                          time_budget_s=None):
     """Run up to `iters` protected iterations (stop early once time_budget_s is spent).
@@ -47,17 +64,7 @@ def protected_iterations(A, B, counts, offsets, tau, mode, zone, base_seed, rank
     t0 = time.perf_counter()
     for it in range(iters):
         C = np.matmul(A, B)
-        seed = orc.inject_seed(base_seed, rank, it)
-        frag = -1
-        if mode in ("add", "swifi"):
-            frag = orc.inject_frag(seed, F)
-            Cf = C[:, offsets[frag]:]
-            if mode == "add":
-                r, c, _ = orc.inject_position(seed, frag, M_b, counts[frag])
-                Cf[r, c] = np.float32(Cf[r, c] + np.float32(1.0e6))
-            else:
-                r, c, b = orc.inject_position(seed, frag, M_b, counts[frag], lo, hi)
-                Cf.view(np.uint32)[r, c] ^= np.uint32(1 << b)
+        frag = inject(C, orc.inject_seed(base_seed, rank, it), counts, offsets, mode, lo, hi)
         c4, n, _, _, _ = orc.verify_iteration(C, A, B, counts, offsets, expRow, tau, frag,
                                               mode in ("add", "swifi"), expCol=None, golden=golden)
         cm += c4
@@ -67,3 +74,33 @@ def protected_iterations(A, B, counts, offsets, tau, mode, zone, base_seed, rank
             break
     secs = time.perf_counter() - t0
     return dict(iters=done, seconds=secs, flops=2.0 * M_b * N_b * K * done, cm=cm.tolist(), n_restored=nr)
+
+
+def abft_only(C_clean, A, B, counts, offsets, tau, mode, zone, base_seed, rank, time_budget_s=5.0, max_reps=5):
+    """The ABFT work alone on the host cores, on a given fault-free C (e.g. the
+    GPU's own SGEMM output): the encode (colSumA, expectedRow) once, then the
+    verification of one iteration (that iteration's planted fault, actualRow +
+    detect on every fragment and the reference's on-demand localisation and
+    correction) repeated on fresh copies until time_budget_s is spent.
+
+    Returns dict(encode_ms, verify_ms (mean per iteration), reps)."""
+    C_clean = np.ascontiguousarray(C_clean, np.float32)
+    A = np.ascontiguousarray(A, np.float32)
+    B = np.ascontiguousarray(B, np.float32)
+    counts = np.ascontiguousarray(counts, np.int32)
+    offsets = np.ascontiguousarray(offsets, np.int32)
+    lo, hi = orc.swifi_zone_range(zone)
+    t0 = time.perf_counter()
+    expRow = orc.expected_row(orc.col_checksum_A(A), B)
+    encode_s = time.perf_counter() - t0
+    total, reps = 0.0, 0
+    while reps < max_reps:
+        C = C_clean.copy()
+        frag = inject(C, orc.inject_seed(base_seed, rank, reps), counts, offsets, mode, lo, hi)
+        t = time.perf_counter()
+        orc.verify_iteration(C, A, B, counts, offsets, expRow, tau, frag, mode in ("add", "swifi"), expCol=None)
+        total += time.perf_counter() - t
+        reps += 1
+        if total >= time_budget_s:
+            break
+    return dict(encode_ms=encode_s * 1e3, verify_ms=total / reps * 1e3, reps=reps)

@@ -74,3 +74,8 @@ def test_sweep_commands_are_valid_driver_invocations(tmp_path):
         assert "flag" not in r.stderr and "must be" not in r.stderr, (label, r.stderr)
     multi = sweep.commands(dict(k, NP=8))
     assert all("--nproc-per-node=8" in argv and DRIVER in argv for _, argv in multi)
+    # the rendezvous port is chosen at launch, one per run
+    assert all(sweep.PORT_ARG in argv for _, argv in multi)
+    launched = sweep.launch_argv(multi[0][1])
+    port = [a for a in launched if a.startswith("--master-port=")]
+    assert len(port) == 1 and int(port[0].split("=")[1]) > 0 and sweep.PORT_ARG not in launched

@@ -6,6 +6,7 @@ import csv
 import os
 import subprocess
 
+import numpy as np
 import pytest
 
 import refharness
@@ -34,6 +35,33 @@ CASES = [
     ["1024", "--calibrate"],
     ["1100", "300", "1030", "--calibrate", "--calibration-safety", "4", "--frags-per-rank", "3"],
 ]
+
+
+# The workloads' own shapes (rank tiles of the tile-geometry table), with the
+# relative threshold 1e-5 * K * max|A| * max|B| computed on the host from the
+# inputs both binaries draw (the reference has no relative-threshold flag, so
+# both get it as --threshold). (label, M, K, N, flags, trial protocol)
+SHAPE_CASES = [
+    ("4096^3 swifi any, F=4, 20 iterations", 4096, 4096, 4096, ["--inject", "swifi", "--swifi-zone", "any"],
+     ["--repeats", "20", "--samples", "1", "--warmups", "1"]),
+    ("16384^3 swifi any, one GPU", 16384, 16384, 16384, ["--inject", "swifi", "--swifi-zone", "any"],
+     ["--repeats", "3", "--samples", "1", "--warmups", "1"]),
+    ("tall 16384x1024 K=4096, add", 16384, 4096, 1024, ["--inject", "add"],
+     ["--repeats", "5", "--samples", "1", "--warmups", "1"]),
+    ("wide 1024x16384 K=16384, add", 1024, 16384, 16384, ["--inject", "add"],
+     ["--repeats", "5", "--samples", "1", "--warmups", "1"]),
+    ("8192^3 2x4 rank-tile shape 4096x2048 K=8192, add", 4096, 8192, 2048, ["--inject", "add"],
+     ["--repeats", "5", "--samples", "1", "--warmups", "1"]),
+]
+
+
+def relative_tau(orc, M, K, N, seed_a=123456, seed_b=987654):
+    A = orc.fill_random(M * K, seed_a)
+    a = float(np.abs(A).max())
+    del A
+    B = orc.fill_random(K * N, seed_b)
+    b = float(np.abs(B).max())
+    return 1e-5 * K * a * b
 
 
 def run(binary, args, csv_path, env_extra=None):
@@ -68,6 +96,22 @@ def test_driver_matches_reference_binary(case, tmp_path):
         assert "Suggested threshold" in out_ours
     else:
         assert "TP / TN / FP / FN" in out_ours
+
+
+@pytest.mark.parametrize("label,M,K,N,flags,protocol", SHAPE_CASES, ids=[c[0] for c in SHAPE_CASES])
+def test_driver_matches_reference_at_workload_shapes(label, M, K, N, flags, protocol, orc, tmp_path):
+    tau = relative_tau(orc, M, K, N)
+    case = [str(M), str(K), str(N)] + flags + ["--threshold", "%.17g" % tau] + protocol
+    ours, out_ours = run(DRIVER, case, str(tmp_path / "ours.csv"))
+    ref, _ = run(refharness.REF_DRIVER, case, str(tmp_path / "ref.csv"))
+    assert list(ours.keys()) == list(ref.keys())
+    for k in ref:
+        if k not in TIMING_COLS:
+            assert ours[k] == ref[k], (k, ours[k], ref[k])
+    tp, fn = int(ours["TP"]), int(ours["FN"])
+    assert tp + fn == int(protocol[1]) * int(protocol[3])  # one injected fragment per recorded iteration
+    if "add" in flags:
+        assert fn == 0 and int(ours["FP"]) == 0
 
 
 def test_driver_rejects_bad_flags(tmp_path):

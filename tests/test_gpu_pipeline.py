@@ -94,6 +94,26 @@ def test_formula_threshold_and_normal_inputs(abft, orc):
     s.close()
 
 
+@pytest.mark.parametrize("M,K,N", [(16384, 4096, 1024), (1024, 16384, 16384)], ids=["tall", "wide"])
+def test_workload_shapes_normal_inputs(M, K, N, abft, orc):
+    """The non-square workload shapes with normal(0,1) inputs (tall: 16384 x
+    1024 tile, K = 4096; wide: 1024 x 16384 tile, K = 16384), F = 4, threshold
+    1e-5 * K * max|A| * max|B|: the reference's additive faults (+1e6) and the
+    workload's +1.0 at a seeded tile-uniform (i, j). The reference cannot draw
+    normal inputs, so the oracle replays every decision on the GPU's own C;
+    counters, logs and final buffers must be bit-identical."""
+    s, A, B, counts, offsets, tau, C0 = make_session(abft, orc, M, K, N, 4, dist="normal", max_iters=8)
+    assert tau[0] == 1e-5 * K * float(np.abs(A).max()) * float(np.abs(B).max())
+    res = s.online("add", base_seed=11, repeats=4, log=True)
+    o = orc.online_loop(C0, A, B, counts, offsets, tau, "add", "any", 1.0e6, 11, 0, 4)
+    compare(s, res, o, 4)
+    assert res["cm"][0] == 4
+    res = s.online("add", add_delta=1.0, base_seed=1, repeats=4, log=True, seed_scheme="tile")
+    o = orc.online_loop(C0, A, B, counts, offsets, tau, "add", "any", 1.0, 1, 0, 4, seed_scheme="tile")
+    compare(s, res, o, 4)
+    s.close()
+
+
 def test_add_delta_one_restores_clean_c(abft, orc):
     """+1.0 faults (the 1024^3 workload's fault size) with a golden C: every
     fault is detected, located and corrected back to within tau of the
