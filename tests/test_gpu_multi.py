@@ -138,3 +138,45 @@ def test_reference_binary_two_ranks(grid, tmp_path):
         if k not in TIMING_COLS:
             assert ours[k] == ref[k], (k, ours[k], ref[k])
     assert (ref["Pr"], ref["Pc"]) == tuple(grid) and int(ref["TP"]) + int(ref["FN"]) == 2 * 6 * 2
+
+
+def relative_tau(n):
+    """1e-5 * K * max|A| * max|B| of the global n^3 inputs both drivers draw."""
+    import numpy as np
+    import oracle
+    a = float(np.abs(oracle.fill_random(n * n, 123456)).max())
+    b = float(np.abs(oracle.fill_random(n * n, 987654)).max())
+    return 1e-5 * n * a * b
+
+
+@pytest.mark.skipif(not os.path.exists(REF_MPI), reason="multi-rank reference driver not built")
+@pytest.mark.skipif(NGPU < 4, reason="needs 4 GPUs")
+@pytest.mark.parametrize("size,inject,repeats", [(8192, "add", 5), (16384, "swifi", 3)], ids=["8192-add", "16384-swifi"])
+def test_reference_binary_all_gpus(size, inject, repeats, tmp_path):
+    """The multi-GPU workloads against the reference driver itself, one rank
+    per GPU on the 2x4 grid (2x2 with 4 GPUs): global 8192^3 with an additive
+    fault on every rank every iteration, and global 16384^3 with SWIFI flips;
+    relative threshold 1e-5 * K * max|A| * max|B| given to both. Every
+    non-timing CSV column (confusion matrix summed over ranks, restore count,
+    threshold, geometry) must be equal."""
+    n = 8 if NGPU >= 8 else 4
+    args = [str(size), "--grid", *GRIDS[n], "--inject", inject, "--threshold", "%.17g" % relative_tau(size),
+            "--repeats", str(repeats), "--samples", "1", "--warmups", "1"]
+    ref_csv, ours_csv = str(tmp_path / "ref.csv"), str(tmp_path / "ours.csv")
+    wrap = 'OMPI_COMM_WORLD_LOCAL_RANK=$LOCAL_RANK exec "$0" "$@"'
+    r = torchrun(n, ["--no-python", "bash", "-c", wrap, REF_MPI] + args + ["--csv", ref_csv], timeout=900,
+                 env_extra={"ABFT_MPI_STUB_PORT": str(free_ports(n)), "ABFT_MPI_STUB_TIMEOUT": "300"})
+    assert r.returncode == 0, (r.stdout[-2000:], r.stderr[-3000:])
+    drv = os.path.join(ROOT, PKG_NAME, "abft_gemm")
+    r = torchrun(n, ["--no-python", drv] + args + ["--csv", ours_csv], timeout=900)
+    assert r.returncode == 0, (r.stdout[-2000:], r.stderr[-3000:])
+    ref = list(csv.DictReader(open(ref_csv)))[0]
+    ours = list(csv.DictReader(open(ours_csv)))[0]
+    assert list(ours.keys()) == list(ref.keys())
+    for k in ref:
+        if k not in TIMING_COLS:
+            assert ours[k] == ref[k], (k, ours[k], ref[k])
+    assert (ref["Pr"], ref["Pc"]) == GRIDS[n]
+    assert int(ref["TP"]) + int(ref["FN"]) == n * repeats  # one injected fragment per rank per iteration
+    if inject == "add":
+        assert int(ref["FN"]) == 0 and int(ref["FP"]) == 0
