@@ -17,9 +17,10 @@ VERIFY_KERNELS = {"auto": 0, "ldg": 1, "tma": 2}
 
 
 def set_verify_kernel(which):
-    """Verify body for every later verify launch in this process: "auto" (by
-    fragment size), "ldg" (128-bit loads) or "tma" (bulk tensor copies through
-    shared memory). Returns the previous setting."""
+    """Verify body for every later verify launch in this process: "auto" (the
+    faster body by fragment size: TMA below 24 MiB, 128-bit loads above), "ldg"
+    (128-bit loads) or "tma" (bulk tensor copies through shared memory).
+    Returns the previous setting."""
     prev = lib.abft_set_verify_kernel(VERIFY_KERNELS[which])
     if prev < 0:
         raise AbftError("abft_set_verify_kernel", prev, _lib.last_error())

@@ -57,10 +57,11 @@ constexpr int kTmaStages = 6;
 constexpr int kStageBytes = kTmaRows * kGroupCols * 4;
 constexpr int kTmaSmem = kTmaStages * kStageBytes;
 constexpr int kTmaAlign = 1024;  // alignment of the ring (bulk tensor copy destinations)
-// Fragments of at least this many bytes use the TMA body by default: measured on
-// B200 with L2 emptied before each launch, the two bodies are within 1 us of
-// each other up to 268 MB (128-bit loads ahead by 2-8 %), TMA ahead by 2 % at 1 GiB.
-constexpr long long kTmaMinBytes = 512LL << 20;
+// The automatic choice takes the TMA body for fragments below this many bytes:
+// measured on B200 with L2 emptied before each launch, it is 0.1-0.9 us ahead
+// from 1 MB to 16.8 MB, while the 128-bit-load body with balanced row units is
+// ahead from 33.6 MB up (2.5 us at 268 MB, 17 us at 1 GiB).
+constexpr long long kTmaMaxBytes = 24LL << 20;
 // Bound of every mbarrier wait (try_wait polls); a wait that runs out records a
 // fault in the counters instead of spinning on.
 constexpr int kSpinLimit = 1 << 20;
@@ -1329,10 +1330,10 @@ int launch_verify(abft_ws* ws, const float* dC, int64_t ldc, int f, double tau, 
     int groups, chunks;
 
     // TMA-staged body: 16-byte aligned fragment, pitch a multiple of 4 floats,
-    // at least one full box; by default for fragments of kTmaMinBytes or more.
+    // at least one full box; when selected, or automatically below kTmaMaxBytes.
     const int choice = g_verify_kernel.load(std::memory_order_relaxed);
     const bool tma_ok = aligned16(Cf) && (ldc % 4 == 0) && N >= kGroupCols && M >= kTmaRows;
-    const bool want_tma = (choice == 2) || (choice == 0 && 4LL * M * N >= kTmaMinBytes);
+    const bool want_tma = (choice == 2) || (choice == 0 && 4LL * M * N < kTmaMaxBytes);
     CUtensorMap map;
     if (tma_ok && want_tma && fragment_tensor_map(&map, Cf, ldc, M, N)) {
         const int per_sm = resident_per_sm((const void*)k_verify_tma, kTmaSmem + kTmaAlign);

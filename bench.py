@@ -78,7 +78,7 @@ def parse():
     p.add_argument("--no-graph", action="store_true", help="enqueue the loop from the host every step")
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--verify-kernel", choices=["auto", "ldg", "tma"], default="auto",
-                   help="verify body: by fragment size, 128-bit loads, or TMA-staged")
+                   help="verify body: auto (the faster one), 128-bit loads, or TMA-staged")
     p.add_argument("--verify-sweep", action="store_true",
                    help="instead of the benchmark: the verify kernel alone on the fragment shapes of the "
                         "workloads (L2 emptied before each launch, mean of 30 launches), one JSON line per shape")
@@ -161,10 +161,14 @@ def peak_hbm():
         return FALLBACK_HBM_GBS, "fallback"
 
 
+TMA_AUTO_MAX_BYTES = 24 << 20  # the library's automatic choice: TMA body below this fragment size
+
+
 def verify_traffic_per_launch(M_b, N_f, kernel):
     """DRAM bytes per verify launch from the committed ncu summary of this
-    fragment shape and verify body, if any."""
-    body = "verify_tma" if kernel == "tma" else "verify"
+    fragment shape and of the verify body that runs it, if any."""
+    tma = kernel == "tma" or (kernel == "auto" and 4 * M_b * N_f < TMA_AUTO_MAX_BYTES)
+    body = "verify_tma" if tma else "verify"
     path = os.path.join(ROOT, "profiles", f"{body}_{M_b}x{N_f}.md")
     try:
         with open(path) as f:
