@@ -28,8 +28,8 @@ static size_t up256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 WsLayout ws_layout(int M_b, int N_b, int K, int F, int nfmax, int max_iters) {
     WsLayout L{};
-    const size_t nfpad = (size_t)((nfmax + kGroupCols - 1) / kGroupCols) * kGroupCols;
-    const size_t groups = nfpad / kGroupCols;
+    const size_t nacc = (size_t)acc_columns(nfmax, K);
+    const size_t groups = nacc / kGroupCols;
     size_t o = 0;
     auto take = [&](size_t bytes) {
         size_t at = o;
@@ -42,12 +42,12 @@ WsLayout ws_layout(int M_b, int N_b, int K, int F, int nfmax, int max_iters) {
     L.expCol = take(sizeof(double) * (size_t)F * M_b);
     L.rec = take(sizeof(FragRecord) * F);
     L.ctr = take(sizeof(Counters));
-    L.vacc_s = take(sizeof(double) * nfpad);
-    L.vacc_t = take(sizeof(float) * nfpad);
-    L.vacc_m = take(sizeof(uint32_t) * nfpad);
-    L.vact = take(sizeof(double) * nfpad);
-    L.vd = take(sizeof(double) * nfpad);
-    L.vw = take(sizeof(double) * nfpad);
+    L.vacc_s = take(sizeof(double) * nacc);
+    L.vacc_t = take(sizeof(float) * nacc);
+    L.vacc_m = take(sizeof(uint32_t) * nacc);
+    L.vact = take(sizeof(double) * nacc);
+    L.vd = take(sizeof(double) * nacc);
+    L.vw = take(sizeof(double) * nacc);
     L.vcnt = take(sizeof(int) * vcnt_ints((int)groups));
     L.lact = take(sizeof(double) * M_b);
     L.ld = take(sizeof(double) * M_b);
@@ -117,7 +117,7 @@ int abft_ws_create(int M_b, int N_b, int K, int F, const int* counts, const int*
     ws->counts.assign(counts, counts + F);
     ws->offsets.assign(offsets, offsets + F);
     ws->nfmax = *std::max_element(ws->counts.begin(), ws->counts.end());
-    ws->nfpad = ((ws->nfmax + kGroupCols - 1) / kGroupCols) * kGroupCols;
+    ws->nacc = acc_columns(ws->nfmax, K);
     cudaError_t e = cudaGetDevice(&ws->device);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&ws->sms, cudaDevAttrMultiProcessorCount, ws->device);
     if (e != cudaSuccess) {
@@ -150,7 +150,7 @@ int abft_ws_create(int M_b, int N_b, int K, int F, const int* counts, const int*
         return cuda_fail(e, "workspace memset");
     }
     char* b = static_cast<char*>(ws->base);
-    e = cudaMemset(b + L.vacc_m, 0xff, sizeof(uint32_t) * ws->nfpad);
+    e = cudaMemset(b + L.vacc_m, 0xff, sizeof(uint32_t) * ws->nacc);
     // The clears run on the legacy default stream and do not block the host;
     // callers launch on their own (possibly non-blocking) streams, which are
     // not ordered after them, so they must be complete before returning.

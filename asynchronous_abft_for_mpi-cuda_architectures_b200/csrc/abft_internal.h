@@ -25,6 +25,12 @@ constexpr int kVerifySmemMax = 64 * 1024;  // verify dynamic shared memory cap
 //   [kArriveGroup + G + g]  next unit of rows of column group g to hand out
 constexpr int kArriveGroup = 2;
 constexpr int vcnt_ints(int groups) { return kArriveGroup + 2 * groups; }
+// Columns of the per-column verify accumulators: the widest fragment, or the
+// K columns of A whose sums the encode takes through the same kernel, rounded
+// up to whole column groups.
+constexpr int acc_columns(int nfmax, int K) {
+    return ((nfmax > K ? nfmax : K) + kGroupCols - 1) / kGroupCols * kGroupCols;
+}
 
 // Per-fragment decision record (the reference's dErrCol[f] / dRowDiff[f],
 // plus the located row).
@@ -76,10 +82,10 @@ struct WsDev {
     Counters* ctr;
     // per-column accumulators of the verify kernel: double sum, float sum of
     // |x| and the smallest (|x| bits - 1) (0xffffffff when every term is 0)
-    double* vacc_s;    // [nfpad]
-    float* vacc_t;     // [nfpad]
-    uint32_t* vacc_m;  // [nfpad]
-    double* vact;      // [nfpad]
+    double* vacc_s;    // [nacc]
+    float* vacc_t;     // [nacc]
+    uint32_t* vacc_m;  // [nacc]
+    double* vact;      // [nacc]
     double* vd;
     double* vw;
     int* vcnt;         // [vcnt_ints(groups_max)], 8-byte aligned
@@ -99,7 +105,7 @@ struct WsDev {
 struct abft_ws {
     int device = 0;
     int sms = 148;
-    int M_b = 0, N_b = 0, K = 0, F = 0, nfmax = 0, nfpad = 0, max_iters = 0;
+    int M_b = 0, N_b = 0, K = 0, F = 0, nfmax = 0, nacc = 0, max_iters = 0;
     std::vector<int> counts, offsets;
     void* base = nullptr;
     size_t bytes = 0;

@@ -465,13 +465,13 @@ __device__ __forceinline__ void verify_tail(unsigned char* dsm, SelectSmem& sel,
     fence_acq_rel_gpu();
 
     // Last CTA of the group: certify its columns, reset their accumulators.
-    double d = 0.0, wv = 0.0;
+    double S = 0.0, d = 0.0, wv = 0.0;
     int cand = 0;
     if (tid < kGroupCols && col < N) {
-        const double S = __ldcg(w.vacc_s + col);
+        S = __ldcg(w.vacc_s + col);
         const float T = __ldcg(w.vacc_t + col);
         const uint32_t mb = __ldcg(w.vacc_m + col);
-        const double E = expv[col];
+        const double E = (expv != nullptr) ? expv[col] : 0.0;
         w.vacc_s[col] = 0.0;
         w.vacc_t[col] = 0.f;
         w.vacc_m[col] = kFull;
@@ -486,17 +486,18 @@ __device__ __forceinline__ void verify_tail(unsigned char* dsm, SelectSmem& sel,
         // Calibration (pass_calibrate, pipeline/passes.cuh:66-84): every
         // |actualRow - expectedRow| exactly, the group's uncertified columns
         // re-summed in the reference's order (one warp per column); no
-        // detection, no counters.
+        // detection, no counters. Without expected checksums (expv null) the
+        // exact column sums themselves (the encode's colSumA).
         if (tid < kGroupCols) sel.d[tid] = (col < N) ? wv : 0.0;
         __syncthreads();
         for (int c = warp; c < kGroupCols; c += kWarps) {
             const int j = g * kGroupCols + c;
             if (j < N && sel.d[c] != 0.0) {
-                const double S = exact_chain(C + j, ldc, M);
-                if (lane == 0) calib_out[j] = fabs(S - expv[j]);
+                const double Sx = exact_chain(C + j, ldc, M);
+                if (lane == 0) calib_out[j] = (expv != nullptr) ? fabs(Sx - expv[j]) : Sx;
             }
         }
-        if (tid < kGroupCols && col < N && wv == 0.0) calib_out[col] = d;
+        if (tid < kGroupCols && col < N && wv == 0.0) calib_out[col] = (expv != nullptr) ? d : S;
         cand = 0;
     }
     // With at most 32 groups the final word's high half is a mask of the
@@ -591,7 +592,7 @@ __global__ void __launch_bounds__(kThreads, 4)
 
     // The expected checksums of this group's columns (1 KB) are read only by
     // the group's last CTA; the group's first CTA pulls them into L2 meanwhile.
-    if (blockIdx.y == 0 && tid < kGroupCols / 16 && g * kGroupCols + tid * 16 < N)
+    if (expv != nullptr && blockIdx.y == 0 && tid < kGroupCols / 16 && g * kGroupCols + tid * 16 < N)
         prefetch_l2(expv + g * kGroupCols + tid * 16);
 
     double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
@@ -735,7 +736,8 @@ __global__ void __launch_bounds__(kThreads, 2)
             tma_load_2d(ring + k * kStageBytes, &tmap, &full[k], gc0, r0 + k * kTmaRows);
         }
     }
-    if (chunk == 0 && tid < kGroupCols / 16 && gc0 + tid * 16 < N) prefetch_l2(expv + gc0 + tid * 16);
+    if (expv != nullptr && chunk == 0 && tid < kGroupCols / 16 && gc0 + tid * 16 < N)
+        prefetch_l2(expv + gc0 + tid * 16);
 
     double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
     float t0 = 0.f, t1 = 0.f, t2 = 0.f, t3 = 0.f;
@@ -824,6 +826,64 @@ __global__ void __launch_bounds__(kThreads, 2)
 
 // ----------------------------------------------------------- localise -----
 
+// Statistics of ROWS rows of X (rows rb, rb + kWarps, ...; those at or past
+// r1 give zeros) over columns [0, N), one warp: per row the double sum S,
+// the float |x|-sum and the smallest (|x| bits - 1), reduced across the warp so
+// that every lane holds them. ROWS rows side by side overlap their loads and
+// add chains (narrow rows); a single row keeps 4 loads per lane in flight
+// along the row (wide rows).
+template <bool VEC, int ROWS>
+__device__ __forceinline__ void row_stats(const float* __restrict__ X, long long ld, int N, int rb, int r1,
+                                          double (&s)[ROWS], float (&t)[ROWS], uint32_t (&m)[ROWS]) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int u = 0; u < ROWS; ++u) {
+        s[u] = 0.0;
+        t[u] = 0.f;
+        m[u] = kFull;
+    }
+    if (VEC) {
+#pragma unroll(ROWS == 1 ? 4 : 2)
+        for (int c = lane * 4; c < N; c += 128) {
+            float4 v[ROWS];
+#pragma unroll
+            for (int u = 0; u < ROWS; ++u) {
+                const int r = rb + u * kWarps;
+                v[u] = (r < r1) ? __ldg(reinterpret_cast<const float4*>(X + (long long)r * ld + c))
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < ROWS; ++u) {
+                acc1(v[u].x, s[u], t[u], m[u]);
+                acc1(v[u].y, s[u], t[u], m[u]);
+                acc1(v[u].z, s[u], t[u], m[u]);
+                acc1(v[u].w, s[u], t[u], m[u]);
+            }
+        }
+    } else {
+#pragma unroll(ROWS == 1 ? 4 : 2)
+        for (int c = lane; c < N; c += 32) {
+            float v[ROWS];
+#pragma unroll
+            for (int u = 0; u < ROWS; ++u) {
+                const int r = rb + u * kWarps;
+                v[u] = (r < r1) ? __ldg(X + (long long)r * ld + c) : 0.f;
+            }
+#pragma unroll
+            for (int u = 0; u < ROWS; ++u) acc1(v[u], s[u], t[u], m[u]);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+        for (int u = 0; u < ROWS; ++u) {
+            s[u] = __dadd_rn(s[u], __shfl_xor_sync(kFull, s[u], o));
+            t[u] += __shfl_xor_sync(kFull, t[u], o);
+            m[u] = min(m[u], __shfl_xor_sync(kFull, m[u], o));
+        }
+    }
+}
+
 // Gated localisation + correction for one fragment: row sums of the fragment
 // (a warp sums ROWS rows side by side), certified like the column sums, then the reference's row
 // arg-max (k_locate_correct) and the correction C = float(double(C) - rowdiff).
@@ -846,52 +906,7 @@ __global__ void __launch_bounds__(kThreads)
         double s[ROWS];
         float t[ROWS];
         uint32_t m[ROWS];
-#pragma unroll
-        for (int u = 0; u < ROWS; ++u) {
-            s[u] = 0.0;
-            t[u] = 0.f;
-            m[u] = kFull;
-        }
-        if (VEC) {
-#pragma unroll(ROWS == 1 ? 4 : 2)
-            for (int c = lane * 4; c < N; c += 128) {
-                float4 v[ROWS];
-#pragma unroll
-                for (int u = 0; u < ROWS; ++u) {
-                    const int r = rb + u * kWarps;
-                    v[u] = (r < r1) ? __ldg(reinterpret_cast<const float4*>(C + (long long)r * ldc + c))
-                                    : make_float4(0.f, 0.f, 0.f, 0.f);
-                }
-#pragma unroll
-                for (int u = 0; u < ROWS; ++u) {
-                    acc1(v[u].x, s[u], t[u], m[u]);
-                    acc1(v[u].y, s[u], t[u], m[u]);
-                    acc1(v[u].z, s[u], t[u], m[u]);
-                    acc1(v[u].w, s[u], t[u], m[u]);
-                }
-            }
-        } else {
-#pragma unroll(ROWS == 1 ? 4 : 2)
-            for (int c = lane; c < N; c += 32) {
-                float v[ROWS];
-#pragma unroll
-                for (int u = 0; u < ROWS; ++u) {
-                    const int r = rb + u * kWarps;
-                    v[u] = (r < r1) ? __ldg(C + (long long)r * ldc + c) : 0.f;
-                }
-#pragma unroll
-                for (int u = 0; u < ROWS; ++u) acc1(v[u], s[u], t[u], m[u]);
-            }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-#pragma unroll
-            for (int u = 0; u < ROWS; ++u) {
-                s[u] = __dadd_rn(s[u], __shfl_xor_sync(kFull, s[u], o));
-                t[u] += __shfl_xor_sync(kFull, t[u], o);
-                m[u] = min(m[u], __shfl_xor_sync(kFull, m[u], o));
-            }
-        }
+        row_stats<VEC, ROWS>(C, ldc, N, rb, r1, s, t, m);
         if (lane < ROWS) {
             // lane u writes row u's results (a select keeps s, t, m in registers)
             double su = s[0];
@@ -947,6 +962,35 @@ __global__ void __launch_bounds__(kThreads)
         }
         w.rec[f].errrow = er;
         if (it >= 0) w.dlog[(long long)it * F + f].errrow = er;
+    }
+}
+
+// Row sums in the reference's order (k_row_checksum_B_g,
+// kernels/abft_stepwise.cuh:121-132: out[r] = sum over c < N of X[r, c],
+// sequential double adds), bit for bit: a warp sums ROWS rows side by side
+// (or one wide row) in any order with the certificate of the verify kernel,
+// and a row whose sum is not certified is re-summed in the reference's order
+// by the whole warp (exact_chain). Encode-time; no gate.
+template <bool VEC, int ROWS>
+__global__ void __launch_bounds__(kThreads)
+    k_rowsum(const float* __restrict__ X, long long ld, int R, int N, int rows_per, double* __restrict__ out) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int r0 = blockIdx.x * rows_per;
+    const int r1 = min(R, r0 + rows_per);
+    for (int rb = r0 + warp; rb < r1; rb += ROWS * kWarps) {
+        double s[ROWS];
+        float t[ROWS];
+        uint32_t m[ROWS];
+        row_stats<VEC, ROWS>(X, ld, N, rb, r1, s, t, m);
+#pragma unroll
+        for (int u = 0; u < ROWS; ++u) {
+            const int r = rb + u * kWarps;
+            if (r < r1) {  // every lane holds the same statistics: warp-uniform branches
+                double S = s[u];
+                if (cert_window(S, t[u], m[u], N, fabs(S)) != 0.0) S = exact_chain(X + (long long)r * ld, 1, N);
+                if (lane == 0) out[r] = S;
+            }
+        }
     }
 }
 
@@ -1008,13 +1052,20 @@ __device__ __forceinline__ void cp_async_wait() {
     asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
 }
 
-constexpr int kColStages = 16;  // 16 x 32 rows x 32 columns x 4 B = 64 KB
-constexpr int kColSmem = kColStages * 32 * 32 * 4;
+// Column chains stage 32-row x 32-column tiles (4 KB) through shared memory:
+// 16 stages (64 KB per one-warp CTA) keep a chain fed best, 6 stages (24 KB)
+// let up to 9 CTAs share an SM, so that many columns still run as one wave
+// (a second wave would double the time of the whole launch).
+constexpr int kColStagesDeep = 16;
+constexpr int kColStagesShallow = 6;
+constexpr int col_smem(int stages) { return stages * 32 * 32 * 4; }
 
-// Column chains: out[c] = sequential sum over rows r of X[r, c] (WEIGHTED:
-// fused multiply-add chain with per-row weight wrow[r]). One warp = 32 columns.
-// Replaces k_col_checksum_A (abft_stepwise.cuh:9-18) and k_expected_row (:31-41).
-template <bool WEIGHTED, bool VEC>
+// Column chains in row order, one warp = 32 columns: out[c] = sum over rows r
+// of X[r, c] (sequential double adds; replaces k_col_checksum_A,
+// abft_stepwise.cuh:9-18) or, WEIGHTED, the fused multiply-add chain of
+// wrow[r] * X[r, c] (nvcc contracts the reference's s += a * b; replaces
+// k_expected_row, :31-41).
+template <bool WEIGHTED, bool VEC, int kColStages>
 __global__ void __launch_bounds__(32)
     k_colchain(const float* __restrict__ X, long long ld, int R, int ncols, const double* __restrict__ wrow,
                double* __restrict__ out) {
@@ -1082,12 +1133,11 @@ __global__ void __launch_bounds__(32)
 constexpr int kRowStages = 8;
 constexpr int kRowAcc = 4;
 
-// Row chains: for a in [0, nacc): out[a*ostride + r] = sequential sum over
-// columns c of X[r, c] (weighted: fused multiply-add with W[a*wstride + c]).
-// One warp = 32 rows; tiles of 32 x 32 staged through padded shared memory.
-// Replaces k_row_checksum_B_g (abft_stepwise.cuh:121-132) and
-// k_expected_col_g (:134-146).
-template <bool WEIGHTED>
+// Row chains: for a in [0, nacc): out[a*ostride + r] = fused multiply-add
+// chain over columns c of X[r, c] * W[a*wstride + c] in column order, four
+// weight vectors per pass. One warp = 32 rows; tiles of 32 x 32 staged
+// through padded shared memory. Replaces k_expected_col_g
+// (abft_stepwise.cuh:134-146).
 __global__ void __launch_bounds__(32)
     k_rowchain(const float* __restrict__ X, long long ld, int R, int L, const double* __restrict__ W,
                long long wstride, int nacc, double* __restrict__ out, long long ostride) {
@@ -1097,8 +1147,8 @@ __global__ void __launch_bounds__(32)
     const int rbase = blockIdx.x * 32;
     const int nrv = min(32, R - rbase);
     const int nblk = (L + 31) / 32;
-    const double* Wg = WEIGHTED ? W + (long long)blockIdx.y * kRowAcc * wstride : nullptr;
-    const int na = WEIGHTED ? min(kRowAcc, nacc - (int)blockIdx.y * kRowAcc) : 1;
+    const double* Wg = W + (long long)blockIdx.y * kRowAcc * wstride;
+    const int na = min(kRowAcc, nacc - (int)blockIdx.y * kRowAcc);
     auto issue = [&](int blk) {
         if (blk < nblk) {
             const int slot = blk % kRowStages;
@@ -1108,12 +1158,10 @@ __global__ void __launch_bounds__(32)
                 const float* src = ok ? (X + (long long)(rbase + rr) * ld + c) : X;
                 cp_async4(&tile[slot][rr][lane], src, ok ? 4 : 0);
             }
-            if (WEIGHTED) {
-                for (int a = 0; a < kRowAcc; ++a) {
-                    const bool ok = (a < na) && (c < L);
-                    const double* src = ok ? (Wg + (long long)a * wstride + c) : W;
-                    cp_async8(&wsm[slot][a][lane], src, ok ? 8 : 0);
-                }
+            for (int a = 0; a < kRowAcc; ++a) {
+                const bool ok = (a < na) && (c < L);
+                const double* src = ok ? (Wg + (long long)a * wstride + c) : W;
+                cp_async8(&wsm[slot][a][lane], src, ok ? 8 : 0);
             }
         }
         cp_async_commit();
@@ -1129,22 +1177,14 @@ __global__ void __launch_bounds__(32)
 #pragma unroll 8
             for (int c = 0; c < 32; ++c) {
                 const double x = (double)tile[slot][lane][c];
-                if (WEIGHTED) {
 #pragma unroll
-                    for (int a = 0; a < kRowAcc; ++a) s[a] = __fma_rn(x, wsm[slot][a][c], s[a]);
-                } else {
-                    s[0] = __dadd_rn(s[0], x);
-                }
+                for (int a = 0; a < kRowAcc; ++a) s[a] = __fma_rn(x, wsm[slot][a][c], s[a]);
             }
         } else {
             for (int c = 0; c < nc; ++c) {
                 const double x = (double)tile[slot][lane][c];
-                if (WEIGHTED) {
 #pragma unroll
-                    for (int a = 0; a < kRowAcc; ++a) s[a] = __fma_rn(x, wsm[slot][a][c], s[a]);
-                } else {
-                    s[0] = __dadd_rn(s[0], x);
-                }
+                for (int a = 0; a < kRowAcc; ++a) s[a] = __fma_rn(x, wsm[slot][a][c], s[a]);
             }
         }
         __syncwarp();
@@ -1263,10 +1303,14 @@ int ensure_kernel_attrs(int device) {
     auto set = [&](const void* fn, int bytes) {
         if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     };
-    set((const void*)k_colchain<false, true>, kColSmem);
-    set((const void*)k_colchain<false, false>, kColSmem);
-    set((const void*)k_colchain<true, true>, kColSmem);
-    set((const void*)k_colchain<true, false>, kColSmem);
+    set((const void*)k_colchain<false, true, kColStagesDeep>, col_smem(kColStagesDeep));
+    set((const void*)k_colchain<false, false, kColStagesDeep>, col_smem(kColStagesDeep));
+    set((const void*)k_colchain<false, true, kColStagesShallow>, col_smem(kColStagesShallow));
+    set((const void*)k_colchain<false, false, kColStagesShallow>, col_smem(kColStagesShallow));
+    set((const void*)k_colchain<true, true, kColStagesDeep>, col_smem(kColStagesDeep));
+    set((const void*)k_colchain<true, false, kColStagesDeep>, col_smem(kColStagesDeep));
+    set((const void*)k_colchain<true, true, kColStagesShallow>, col_smem(kColStagesShallow));
+    set((const void*)k_colchain<true, false, kColStagesShallow>, col_smem(kColStagesShallow));
     set((const void*)k_verify<true>, kVerifySmemMax);
     set((const void*)k_verify<false>, kVerifySmemMax);
     set((const void*)k_verify_tma, kTmaSmem + kTmaAlign);
@@ -1275,41 +1319,74 @@ int ensure_kernel_attrs(int device) {
     return ABFT_OK;
 }
 
+// Rows per CTA of the row-sum kernels (localise, encode): about 64 KB of the
+// matrix per CTA, but no more rows than give two CTAs per SM (whole warps of
+// rows, 8 to 256 rows).
+int row_block(int R, int N, int sms) {
+    long long rows = 65536 / ((long long)N * 4);
+    rows = std::min(rows, (long long)((R + 2 * sms - 1) / (2 * sms)));
+    if (rows < kWarps) rows = kWarps;
+    if (rows > 256) rows = 256;
+    return (int)((rows + kWarps - 1) / kWarps) * kWarps;
+}
+
 int launch_encode(abft_ws* ws, const float* dA, int64_t lda, const float* dB, int64_t ldb, cudaStream_t st,
                   int* launches) {
     if (int rc = ensure_kernel_attrs(ws->device)) return rc;
     const int M = ws->M_b, K = ws->K, N = ws->N_b, F = ws->F;
     int n = 0;
-    // colSumA[K]: chains over the M rows of A.
-    {
-        const bool vec = aligned16(dA) && (lda % 4 == 0);
-        dim3 grid((K + 31) / 32);
-        if (vec) k_colchain<false, true><<<grid, 32, kColSmem, st>>>(dA, lda, M, K, nullptr, ws->d.colSumA);
-        else k_colchain<false, false><<<grid, 32, kColSmem, st>>>(dA, lda, M, K, nullptr, ws->d.colSumA);
-        ++n;
-        if (int rc = check_launch("encode colSumA")) return rc;
-    }
+    // Column chains of K columns over R rows, as one wave of one-warp CTAs.
+    auto colchain = [&](bool weighted, const float* X, int64_t ld, int R, int ncols, const double* wrow,
+                        double* out) {
+        const bool vec = aligned16(X) && (ld % 4 == 0);
+        const int ctas = (ncols + 31) / 32;
+        const bool deep = ctas <= ws->sms * (227 * 1024 / col_smem(kColStagesDeep));
+        const dim3 grid(ctas);
+#define ABFT_COLCHAIN(W, V, S) k_colchain<W, V, S><<<grid, 32, col_smem(S), st>>>(X, ld, R, ncols, wrow, out)
+#define ABFT_COLCHAIN_STAGES(W, V) \
+    do {                           \
+        if (deep)                  \
+            ABFT_COLCHAIN(W, V, kColStagesDeep); \
+        else                       \
+            ABFT_COLCHAIN(W, V, kColStagesShallow); \
+    } while (0)
+        if (weighted && vec) ABFT_COLCHAIN_STAGES(true, true);
+        else if (weighted) ABFT_COLCHAIN_STAGES(true, false);
+        else if (vec) ABFT_COLCHAIN_STAGES(false, true);
+        else ABFT_COLCHAIN_STAGES(false, false);
+#undef ABFT_COLCHAIN_STAGES
+#undef ABFT_COLCHAIN
+    };
+    // colSumA[K]: sequential chains over the M rows of A. (A certified
+    // parallel sum, as verify uses, loses here at large M: one tiny element
+    // among M uniform terms sets the certificate's exponent, and at M = 16384
+    // about 12 % of columns fail it and need the sequential re-sum anyway.)
+    colchain(false, dA, lda, M, K, nullptr, ws->d.colSumA);
+    ++n;
+    if (int rc = check_launch("encode colSumA")) return rc;
     // expRow[N_b]: fused multiply-add chains over the K rows of B.
-    {
-        const bool vec = aligned16(dB) && (ldb % 4 == 0);
-        dim3 grid((N + 31) / 32);
-        if (vec) k_colchain<true, true><<<grid, 32, kColSmem, st>>>(dB, ldb, K, N, ws->d.colSumA, ws->d.expRow);
-        else k_colchain<true, false><<<grid, 32, kColSmem, st>>>(dB, ldb, K, N, ws->d.colSumA, ws->d.expRow);
-        ++n;
-        if (int rc = check_launch("encode expectedRow")) return rc;
-    }
-    // rowSumB_f[K] per fragment: chains over the fragment's columns of each B row.
+    colchain(true, dB, ldb, K, N, ws->d.colSumA, ws->d.expRow);
+    ++n;
+    if (int rc = check_launch("encode expectedRow")) return rc;
+    // rowSumB_f[K] per fragment: certified row sums over the fragment's columns of each B row.
     for (int f = 0; f < F; ++f) {
-        dim3 grid((K + 31) / 32, 1);
-        k_rowchain<false><<<grid, 32, 0, st>>>(dB + ws->offsets[f], ldb, K, ws->counts[f], nullptr, 0, 1,
-                                               ws->d.rowSumB + (long long)f * K, 0);
+        const float* Bf = dB + ws->offsets[f];
+        const int Nf = ws->counts[f];
+        const int rows_per = row_block(K, Nf, ws->sms);
+        const int nblocks = (K + rows_per - 1) / rows_per;
+        const bool vec = aligned16(Bf) && (ldb % 4 == 0) && (Nf % 4 == 0);
+        double* out = ws->d.rowSumB + (long long)f * K;
+        if (vec && Nf <= kLocNarrow) k_rowsum<true, 4><<<nblocks, kThreads, 0, st>>>(Bf, ldb, K, Nf, rows_per, out);
+        else if (vec) k_rowsum<true, 1><<<nblocks, kThreads, 0, st>>>(Bf, ldb, K, Nf, rows_per, out);
+        else if (Nf <= kLocNarrow) k_rowsum<false, 4><<<nblocks, kThreads, 0, st>>>(Bf, ldb, K, Nf, rows_per, out);
+        else k_rowsum<false, 1><<<nblocks, kThreads, 0, st>>>(Bf, ldb, K, Nf, rows_per, out);
         ++n;
         if (int rc = check_launch("encode rowSumB")) return rc;
     }
     // expCol_f[M_b]: fused multiply-add chains over each A row, four fragments per pass.
     {
         dim3 grid((M + 31) / 32, (F + kRowAcc - 1) / kRowAcc);
-        k_rowchain<true><<<grid, 32, 0, st>>>(dA, lda, M, K, ws->d.rowSumB, K, F, ws->d.expCol, M);
+        k_rowchain<<<grid, 32, 0, st>>>(dA, lda, M, K, ws->d.rowSumB, K, F, ws->d.expCol, M);
         ++n;
         if (int rc = check_launch("encode expectedCol")) return rc;
     }
@@ -1365,13 +1442,7 @@ int launch_localize(abft_ws* ws, float* dC, int64_t ldc, int f, double tau, int 
                     int64_t ldg, int it, int correct_mode, cudaStream_t st, int plan_it) {
     const int M = ws->M_b, N = ws->counts[f];
     float* Cf = dC + ws->offsets[f];
-    // about 64 KB of C per CTA, but no more rows than give two CTAs per SM
-    // (whole warps of rows, 8 to 256 rows)
-    long long rows = 65536 / ((long long)N * 4);
-    rows = std::min(rows, (long long)((M + 2 * ws->sms - 1) / (2 * ws->sms)));
-    if (rows < kWarps) rows = kWarps;
-    if (rows > 256) rows = 256;
-    const int rows_per = (int)((rows + kWarps - 1) / kWarps) * kWarps;
+    const int rows_per = row_block(M, N, ws->sms);
     const int nblocks = (M + rows_per - 1) / rows_per;
     const bool vec = aligned16(Cf) && (ldc % 4 == 0) && (N % 4 == 0);
     const double* expc = ws->d.expCol + (long long)f * M;

@@ -412,6 +412,39 @@ def test_exact_chain_adversarial_columns(M, abft, orc, torch_cuda):
     ws.close()
 
 
+@pytest.mark.parametrize("M,K,N,F", [(3000, 257, 1200, 3), (300, 1536, 700, 2)])
+def test_encode_adversarial_sums(M, K, N, F, abft, orc, torch_cuda):
+    """rowSumB_f runs as certified parallel row sums (per warp) with the
+    reference-order re-sum for rows the certificate does not cover. Rows of B
+    and columns of A built to defeat the certificate (tiny, huge, subnormal,
+    cancelling, absorbed terms) must give checksums bit-identical to the
+    reference's sequential ones, and so must the FMA chains that use them as
+    weights."""
+    torch = torch_cuda
+    rng = np.random.default_rng(4040 + M)
+    A = np.empty((M, K), np.float32)
+    for k in range(K):
+        A[:, k] = adversarial(rng, M, k % 13)
+    B = np.empty((K, N), np.float32)
+    for k in range(K):
+        B[k, :] = adversarial(rng, N, (3 * k) % 13)
+    counts, offsets = orc.split_dim(N, F)
+    ws = abft.kernels.Workspace(M, N, K, counts, offsets)
+    abft.kernels.encode(ws, to_dev(torch, A), to_dev(torch, B))
+    torch.cuda.synchronize()
+    got = ws.read_checksums()
+    want = orc.encode(A, B, counts, offsets)
+    for g, w, name in zip(got, want, ["colSumA", "expRow", "rowSumB", "expCol"]):
+        assert np.array_equal(g.view(np.uint64), w.view(np.uint64)), name
+    # the patterns make the order matter: the reference's sequential row sums
+    # differ from the exactly rounded ones in some rows of B
+    import math
+    seq = orc.row_checksum_B(B[:, offsets[0]:offsets[0] + counts[0]])
+    exact = np.array([math.fsum(B[k, offsets[0]:offsets[0] + counts[0]].astype(np.float64)) for k in range(K)])
+    assert (seq != exact).any()
+    ws.close()
+
+
 def test_exact_chain_adversarial_rows(abft, orc, torch_cuda):
     """The same patterns along rows, with a fault to localise: the row arg-max
     re-sums its uncertified candidate rows exactly."""
