@@ -18,7 +18,7 @@ VERIFY_KERNELS = {"auto": 0, "ldg": 1, "tma": 2}
 
 def set_verify_kernel(which):
     """Verify body for every later verify launch in this process: "auto" (the
-    faster body by fragment size: TMA below 24 MiB, 128-bit loads above), "ldg"
+    body that is faster inside the protected loop: 128-bit loads), "ldg"
     (128-bit loads) or "tma" (bulk tensor copies through shared memory).
     Returns the previous setting."""
     prev = lib.abft_set_verify_kernel(VERIFY_KERNELS[which])

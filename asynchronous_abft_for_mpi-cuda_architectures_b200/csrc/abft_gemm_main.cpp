@@ -48,6 +48,7 @@ struct Config {
     float add_delta = ABFT_ADD_FAULT_DELTA;
     int correct_mode = ABFT_CORRECT_INLOOP;
     int verify_priority = -1;
+    int verify_kernel = ABFT_VERIFY_AUTO;
     double relative_threshold = -1.0;  // tau = r * K * max|A| * max|B|
     bool csv_extra = false;
     bool graph = false;
@@ -83,6 +84,7 @@ void print_help() {
         "  --relative-threshold R         tau = R * K * max|A| * max|B|\n"
         "  --correct {inloop|drain}       correct inside the loop or after it\n"
         "  --verify-priority {low|default|high}\n"
+        "  --verify-kernel {auto|ldg|tma} verify body (default auto)\n"
         "  --csv-extra                    append run-setting columns, encode_ms and the corrected C's\n"
         "                                 max relative error against the fault-free SGEMM to the CSV\n"
         "  --graph                        replay each trial's loop as a CUDA graph\n"
@@ -130,6 +132,12 @@ bool parse(int argc, char** argv, Config& c, std::string& err) {
             else if (m == "default") c.verify_priority = 0;
             else if (m == "high") c.verify_priority = 1;
             else { err = "--verify-priority must be low, default or high"; return false; }
+        } else if (a == "--verify-kernel" && need(1)) {
+            std::string m = argv[++i];
+            if (m == "auto") c.verify_kernel = ABFT_VERIFY_AUTO;
+            else if (m == "ldg") c.verify_kernel = ABFT_VERIFY_LDG;
+            else if (m == "tma") c.verify_kernel = ABFT_VERIFY_TMA;
+            else { err = "--verify-kernel must be auto, ldg or tma"; return false; }
         } else if (a == "--csv-extra") c.csv_extra = true;
         else if (a == "--graph") c.graph = true;
         else if (a == "--inject-seed-mode" && need(1)) {
@@ -191,6 +199,7 @@ int main(int argc, char** argv) {
     Config cfg;
     std::string perr;
     if (!parse(argc, argv, cfg, perr)) return die(perr, 2);
+    abft_set_verify_kernel(cfg.verify_kernel);
 
     const RankEnv env = rank_env_from_environment();
     const int world_rank = env.rank, world_size = env.world;

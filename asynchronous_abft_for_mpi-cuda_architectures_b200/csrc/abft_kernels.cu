@@ -57,11 +57,14 @@ constexpr int kTmaStages = 6;
 constexpr int kStageBytes = kTmaRows * kGroupCols * 4;
 constexpr int kTmaSmem = kTmaStages * kStageBytes;
 constexpr int kTmaAlign = 1024;  // alignment of the ring (bulk tensor copy destinations)
-// The automatic choice takes the TMA body for fragments below this many bytes:
-// measured on B200 with L2 emptied before each launch, it is 0.1-0.9 us ahead
-// from 1 MB to 16.8 MB, while the 128-bit-load body with balanced row units is
-// ahead from 33.6 MB up (2.5 us at 268 MB, 17 us at 1 GiB).
-constexpr long long kTmaMaxBytes = 24LL << 20;
+// The automatic choice never takes the TMA body. Timed alone on B200 it is
+// 0.1-0.9 us ahead below 17 MB and behind from 33.6 MB up (2.5 us at 268 MB,
+// 17 us at 1 GiB), but inside the protected loop, where verify runs beside
+// the SGEMM, its ~97 KB of shared memory per CTA keeps it off the SMs the
+// SGEMM occupies: the loop's overhead was higher with it at every measured
+// workload (1024^3 to 16384^3, graph mode), while the 16 KB CTAs of the
+// 128-bit-load body fit beside the SGEMM's.
+constexpr long long kTmaMaxBytes = 0;
 // Bound of every mbarrier wait (try_wait polls); a wait that runs out records a
 // fault in the counters instead of spinning on.
 constexpr int kSpinLimit = 1 << 20;
@@ -1407,7 +1410,7 @@ int launch_verify(abft_ws* ws, const float* dC, int64_t ldc, int f, double tau, 
     int groups, chunks;
 
     // TMA-staged body: 16-byte aligned fragment, pitch a multiple of 4 floats,
-    // at least one full box; when selected, or automatically below kTmaMaxBytes.
+    // at least one full box; when selected explicitly.
     const int choice = g_verify_kernel.load(std::memory_order_relaxed);
     const bool tma_ok = aligned16(Cf) && (ldc % 4 == 0) && N >= kGroupCols && M >= kTmaRows;
     const bool want_tma = (choice == 2) || (choice == 0 && 4LL * M * N < kTmaMaxBytes);

@@ -161,14 +161,11 @@ def peak_hbm():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-TMA_AUTO_MAX_BYTES = 24 << 20  # the library's automatic choice: TMA body below this fragment size
-
-
 def verify_traffic_per_launch(M_b, N_f, kernel):
     """DRAM bytes per verify launch from the committed ncu summary of this
-    fragment shape and of the verify body that runs it, if any."""
-    tma = kernel == "tma" or (kernel == "auto" and 4 * M_b * N_f < TMA_AUTO_MAX_BYTES)
-    body = "verify_tma" if tma else "verify"
+    fragment shape and of the verify body that runs it (the library's
+    automatic choice is the 128-bit-load body), if any."""
+    body = "verify_tma" if kernel == "tma" else "verify"
     path = os.path.join(ROOT, "profiles", f"{body}_{M_b}x{N_f}.md")
     try:
         with open(path) as f:

@@ -175,8 +175,8 @@ int abft_verify_noalloc(const float* dC_frag, int64_t ldc, int M, int N, const d
                         int injected, int* dErrCol, double* dRowDiff, int* dCM, void* stream);
 
 /* Which body abft_verify (and the pipeline) uses for the column sums:
- * ABFT_VERIFY_AUTO picks the faster body by fragment size (on B200: TMA below
- * 24 MiB, 128-bit loads from there up), ABFT_VERIFY_LDG streams the tile
+ * ABFT_VERIFY_AUTO picks the body that is faster inside the protected loop
+ * (on B200: 128-bit loads at every size), ABFT_VERIFY_LDG streams the tile
  * with 128-bit loads, ABFT_VERIFY_TMA stages it through shared memory with
  * bulk tensor copies (falls back to LDG where a tensor map cannot describe
  * the fragment: unaligned base or pitch, fewer than 128 columns or 32 rows).
