@@ -82,7 +82,7 @@ struct abft_session {
     cudaEvent_t in_a[2] = {nullptr, nullptr};
     std::vector<cudaEvent_t> in_b[2];
     cudaEvent_t in_free_c[2] = {nullptr, nullptr}, in_free_v[2] = {nullptr, nullptr};
-    cudaEvent_t d2h_done[2] = {nullptr, nullptr};
+    std::vector<cudaEvent_t> d2h_frag[2];  // result copy of fragment f out of C buffer q done
     cudaEvent_t vstep = nullptr, ojoin = nullptr;
     Counters* ctr_host = nullptr;
     int ctr_host_n = 0;
@@ -158,8 +158,11 @@ struct IoHooks {
     // run_host_steps: both C buffers were used by an earlier step, so their
     // first use here waits for that step's verification of them ...
     bool carry_used = false;
-    // ... and, where not null, for the result copy that read them
-    const cudaEvent_t* slot_free = nullptr;
+    // ... and, where slot_free[buffer] is not null, fragment f's first SGEMM
+    // into that buffer waits for slot_free[buffer][f], the earlier step's copy
+    // of that fragment to the host (not for the copies of the fragments after
+    // it, which start only at the end of that step)
+    const cudaEvent_t* const* slot_free = nullptr;
 };
 
 // Graph mode: a conditional handle of the graph being captured on st, reset
@@ -220,8 +223,7 @@ int enqueue_loop(abft_session* s, const abft_online_args* a, const std::vector<P
         const int bi = it & 1;
         float* dC = s->dC[bi];
         if (used[bi]) CK(cudaStreamWaitEvent(s->compute, s->buf_done[bi], 0));
-        if (first[bi] && io && io->slot_free && io->slot_free[bi])
-            CK(cudaStreamWaitEvent(s->compute, io->slot_free[bi], 0));
+        const cudaEvent_t* slot_free = (first[bi] && io && io->slot_free) ? io->slot_free[bi] : nullptr;
         first[bi] = false;
         const int log_it = (a->log && it < s->max_iters) ? it : -1;
         for (int f = 0; f < s->F; ++f) {
@@ -229,6 +231,7 @@ int enqueue_loop(abft_session* s, const abft_online_args* a, const std::vector<P
                 if (f == 0) CK(cudaStreamWaitEvent(s->compute, io->a_ready, 0));
                 CK(cudaStreamWaitEvent(s->compute, io->b_ready[f], 0));
             }
+            if (slot_free) CK(cudaStreamWaitEvent(s->compute, slot_free[f], 0));
             RC(sgemm_frag(s, dC, f));
             if (!graph && f == plan[it].frag) {
                 InjectLog* lg = (log_it >= 0) ? s->ws->d.ilog + log_it : nullptr;
@@ -395,9 +398,10 @@ int ensure_step_resources(abft_session* s, int n_steps) {
         CK(event(&s->in_a[q]));
         CK(event(&s->in_free_c[q]));
         CK(event(&s->in_free_v[q]));
-        CK(event(&s->d2h_done[q]));
         if ((int)s->in_b[q].size() != s->F) s->in_b[q].assign(s->F, nullptr);
         for (int f = 0; f < s->F; ++f) CK(event(&s->in_b[q][f]));
+        if ((int)s->d2h_frag[q].size() != s->F) s->d2h_frag[q].assign(s->F, nullptr);
+        for (int f = 0; f < s->F; ++f) CK(event(&s->d2h_frag[q][f]));
     }
     CK(event(&s->vstep));
     CK(event(&s->ojoin));
@@ -530,9 +534,11 @@ int abft_session_destroy(abft_session* s) {
     if (s->body) cudaStreamDestroy(s->body);
     if (s->xout) cudaStreamDestroy(s->xout);
     for (int q = 0; q < 2; ++q) {
-        for (auto e : {s->in_a[q], s->in_free_c[q], s->in_free_v[q], s->d2h_done[q]})
+        for (auto e : {s->in_a[q], s->in_free_c[q], s->in_free_v[q]})
             if (e) cudaEventDestroy(e);
         for (auto e : s->in_b[q])
+            if (e) cudaEventDestroy(e);
+        for (auto e : s->d2h_frag[q])
             if (e) cudaEventDestroy(e);
     }
     for (auto e : {s->vstep, s->ojoin})
@@ -925,8 +931,8 @@ int abft_session_run_host_steps(abft_session* s, int n_steps, const float* const
             CK(cudaStreamWaitEvent(s->verify, s->in_b[q][s->F - 1], 0));
             RC(launch_encode(s->ws, inA[q], s->lda, inB[q], s->ldb, s->verify, &nl));
             CK(cudaEventRecord(s->in_free_v[q], s->verify));
-            const cudaEvent_t slot_free[2] = {pending[0] ? s->d2h_done[0] : nullptr,
-                                              pending[1] ? s->d2h_done[1] : nullptr};
+            const cudaEvent_t* const slot_free[2] = {pending[0] ? s->d2h_frag[0].data() : nullptr,
+                                                     pending[1] ? s->d2h_frag[1].data() : nullptr};
             IoHooks io{s->in_a[q], s->in_b[q].data(), drain ? nullptr : s->c_out.data(), k > 0, slot_free};
             ak.base_seed = base_seeds[k];
             RC(enqueue_loop(s, &ak, plans[k], &nl2, &nv, false, &io));
@@ -949,8 +955,8 @@ int abft_session_run_host_steps(abft_session* s, int n_steps, const float* const
                 if (!drain) CK(cudaStreamWaitEvent(s->xout, s->c_out[f], 0));
                 CK(cudaMemcpy2DAsync(hC[k] + off, sizeof(float) * s->N_b, last + off, sizeof(float) * s->ldc,
                                      sizeof(float) * s->counts[f], s->M_b, cudaMemcpyDeviceToHost, s->xout));
+                CK(cudaEventRecord(s->d2h_frag[fin][f], s->xout));
             }
-            CK(cudaEventRecord(s->d2h_done[fin], s->xout));
             pending[fin] = true;
             pending[1 - fin] = false;
         }
