@@ -28,7 +28,7 @@ static size_t up256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 WsLayout ws_layout(int M_b, int N_b, int K, int F, int nfmax, int max_iters) {
     WsLayout L{};
-    const size_t nacc = (size_t)acc_columns(nfmax, K);
+    const size_t nacc = (size_t)acc_columns(nfmax);
     const size_t groups = nacc / kGroupCols;
     size_t o = 0;
     auto take = [&](size_t bytes) {
@@ -117,7 +117,7 @@ int abft_ws_create(int M_b, int N_b, int K, int F, const int* counts, const int*
     ws->counts.assign(counts, counts + F);
     ws->offsets.assign(offsets, offsets + F);
     ws->nfmax = *std::max_element(ws->counts.begin(), ws->counts.end());
-    ws->nacc = acc_columns(ws->nfmax, K);
+    ws->nacc = acc_columns(ws->nfmax);
     cudaError_t e = cudaGetDevice(&ws->device);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&ws->sms, cudaDevAttrMultiProcessorCount, ws->device);
     if (e != cudaSuccess) {

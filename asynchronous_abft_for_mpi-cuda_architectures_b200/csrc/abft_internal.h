@@ -25,12 +25,9 @@ constexpr int kVerifySmemMax = 64 * 1024;  // verify dynamic shared memory cap
 //   [kArriveGroup + G + g]  next unit of rows of column group g to hand out
 constexpr int kArriveGroup = 2;
 constexpr int vcnt_ints(int groups) { return kArriveGroup + 2 * groups; }
-// Columns of the per-column verify accumulators: the widest fragment, or the
-// K columns of A whose sums the encode takes through the same kernel, rounded
-// up to whole column groups.
-constexpr int acc_columns(int nfmax, int K) {
-    return ((nfmax > K ? nfmax : K) + kGroupCols - 1) / kGroupCols * kGroupCols;
-}
+// Columns of the per-column verify accumulators: the widest fragment,
+// rounded up to whole column groups.
+constexpr int acc_columns(int nfmax) { return (nfmax + kGroupCols - 1) / kGroupCols * kGroupCols; }
 
 // Per-fragment decision record (the reference's dErrCol[f] / dRowDiff[f],
 // plus the located row).

@@ -474,7 +474,7 @@ __device__ __forceinline__ void verify_tail(unsigned char* dsm, SelectSmem& sel,
         S = __ldcg(w.vacc_s + col);
         const float T = __ldcg(w.vacc_t + col);
         const uint32_t mb = __ldcg(w.vacc_m + col);
-        const double E = (expv != nullptr) ? expv[col] : 0.0;
+        const double E = expv[col];
         w.vacc_s[col] = 0.0;
         w.vacc_t[col] = 0.f;
         w.vacc_m[col] = kFull;
@@ -489,18 +489,17 @@ __device__ __forceinline__ void verify_tail(unsigned char* dsm, SelectSmem& sel,
         // Calibration (pass_calibrate, pipeline/passes.cuh:66-84): every
         // |actualRow - expectedRow| exactly, the group's uncertified columns
         // re-summed in the reference's order (one warp per column); no
-        // detection, no counters. Without expected checksums (expv null) the
-        // exact column sums themselves (the encode's colSumA).
+        // detection, no counters.
         if (tid < kGroupCols) sel.d[tid] = (col < N) ? wv : 0.0;
         __syncthreads();
         for (int c = warp; c < kGroupCols; c += kWarps) {
             const int j = g * kGroupCols + c;
             if (j < N && sel.d[c] != 0.0) {
                 const double Sx = exact_chain(C + j, ldc, M);
-                if (lane == 0) calib_out[j] = (expv != nullptr) ? fabs(Sx - expv[j]) : Sx;
+                if (lane == 0) calib_out[j] = fabs(Sx - expv[j]);
             }
         }
-        if (tid < kGroupCols && col < N && wv == 0.0) calib_out[col] = (expv != nullptr) ? d : S;
+        if (tid < kGroupCols && col < N && wv == 0.0) calib_out[col] = d;
         cand = 0;
     }
     // With at most 32 groups the final word's high half is a mask of the
@@ -595,7 +594,7 @@ __global__ void __launch_bounds__(kThreads, 4)
 
     // The expected checksums of this group's columns (1 KB) are read only by
     // the group's last CTA; the group's first CTA pulls them into L2 meanwhile.
-    if (expv != nullptr && blockIdx.y == 0 && tid < kGroupCols / 16 && g * kGroupCols + tid * 16 < N)
+    if (blockIdx.y == 0 && tid < kGroupCols / 16 && g * kGroupCols + tid * 16 < N)
         prefetch_l2(expv + g * kGroupCols + tid * 16);
 
     double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
@@ -739,8 +738,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             tma_load_2d(ring + k * kStageBytes, &tmap, &full[k], gc0, r0 + k * kTmaRows);
         }
     }
-    if (expv != nullptr && chunk == 0 && tid < kGroupCols / 16 && gc0 + tid * 16 < N)
-        prefetch_l2(expv + gc0 + tid * 16);
+    if (chunk == 0 && tid < kGroupCols / 16 && gc0 + tid * 16 < N) prefetch_l2(expv + gc0 + tid * 16);
 
     double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
     float t0 = 0.f, t1 = 0.f, t2 = 0.f, t3 = 0.f;
