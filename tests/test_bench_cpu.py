@@ -105,3 +105,17 @@ def test_verify_traffic_comes_from_the_committed_summary():
         t = bench.verify_traffic_per_launch(4096, 1024, kernel)
         assert t is not None and 16.8e6 < t < 16.9e6, (kernel, t)
     assert bench.verify_traffic_per_launch(1234, 4, "auto") is None
+
+
+def test_headline_fragments_have_committed_traffic():
+    """Every fragment shape the headline workload runs at 1, 2, 4 and 8 GPUs
+    has a committed ncu summary whose DRAM traffic is within 3 % of its
+    algorithmic bytes (the excess is DRAM writes: lines that the buffer
+    written to empty L2 left dirty, written back during the launch), so each
+    N's bench line carries roofline.traffic."""
+    sys.path.insert(0, ROOT)
+    import bench
+    for M_b, N_f in [(16384, 4096), (16384, 2048), (8192, 2048), (8192, 1024)]:
+        t = bench.verify_traffic_per_launch(M_b, N_f, "auto")
+        alg = 4.0 * M_b * N_f + 24.0 * N_f
+        assert t is not None and alg <= t <= 1.03 * alg, (M_b, N_f, t, alg)
