@@ -9,7 +9,7 @@ built library raises ImportError; there is no CPU fallback.
 from ._lib import (ADD_FAULT_DELTA, CORRECT_DRAIN, CORRECT_INLOOP, DRIVER_PATH, HEADER_PATH, INJECT_ADD,
                    INJECT_NONE, INJECT_SWIFI, LIB_PATH, SIGNATURES, AbftError, call, lib)
 from . import _lib, host
-from .host import (choose_grid, fill_random, frag_count, frag_thresholds, injection_plan, rank_tile,
+from .host import (c_pitch, choose_grid, fill_random, frag_count, frag_thresholds, injection_plan, rank_tile,
                    relative_threshold, split_dim, swifi_zone_range, threshold_formula)
 
 
@@ -30,7 +30,7 @@ def set_verify_kernel(which):
 __all__ = [
     "ADD_FAULT_DELTA", "CORRECT_DRAIN", "CORRECT_INLOOP", "DRIVER_PATH", "HEADER_PATH", "INJECT_ADD", "INJECT_NONE",
     "INJECT_SWIFI", "LIB_PATH", "SIGNATURES", "AbftError", "lib", "host", "choose_grid", "fill_random",
-    "frag_count", "frag_thresholds", "injection_plan", "rank_tile", "relative_threshold", "split_dim",
+    "c_pitch", "frag_count", "frag_thresholds", "injection_plan", "rank_tile", "relative_threshold", "split_dim",
     "swifi_zone_range", "threshold_formula", "call", "set_verify_kernel", "VERIFY_KERNELS",
 ]
 

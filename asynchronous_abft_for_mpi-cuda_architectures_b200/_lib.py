@@ -102,6 +102,7 @@ SIGNATURES = {
     "abft_choose_grid": (_I, [_I, _IP, _IP]),
     "abft_split_dim": (_I, [_I, _I, _IP, _IP]),
     "abft_frag_count": (_I, [_I, _I, _I, _I, _I, _I, _I64]),
+    "abft_c_pitch": (_I64, [_I]),
     "abft_matrix_inf_norm": (_D, [_P, _I, _I, _I64]),
     "abft_threshold_formula": (_D, [_I, _D, _D]),
     "abft_frag_thresholds": (_I, [_P, _I, _I, _I64, _P, _I64, _I, _IP, _IP, _D, _DP]),

@@ -256,14 +256,17 @@ int main(int argc, char** argv) {
     float *dA = nullptr, *dB = nullptr, *dC0 = nullptr, *dC1 = nullptr, *dG = nullptr, *dStage = nullptr;
     CUDA_TRY(cudaMalloc(&dA, sizeof(float) * (size_t)M_b * K));
     CUDA_TRY(cudaMalloc(&dB, sizeof(float) * (size_t)K * N_b));
-    CUDA_TRY(cudaMalloc(&dC0, sizeof(float) * (size_t)M_b * N_b));
-    CUDA_TRY(cudaMalloc(&dC1, sizeof(float) * (size_t)M_b * N_b));
+    // C buffers at the pipeline's row pitch (padded where a dense one would
+    // slow the verify kernel, abft_c_pitch)
+    const int64_t ldc = abft_c_pitch(N_b);
+    CUDA_TRY(cudaMalloc(&dC0, sizeof(float) * (size_t)M_b * (size_t)ldc));
+    CUDA_TRY(cudaMalloc(&dC1, sizeof(float) * (size_t)M_b * (size_t)ldc));
 
     abft_session_cfg scfg{};
     scfg.M_b = M_b; scfg.N_b = N_b; scfg.K = K; scfg.F = F;
     scfg.counts = fc.data(); scfg.offsets = fo.data();
     scfg.dA = dA; scfg.lda = K; scfg.dB = dB; scfg.ldb = N_b;
-    scfg.dC0 = dC0; scfg.dC1 = dC1; scfg.ldc = N_b;
+    scfg.dC0 = dC0; scfg.dC1 = dC1; scfg.ldc = ldc;
     scfg.verify_priority = cfg.verify_priority;
     scfg.max_iters = cfg.repeats;
     abft_session* sess = nullptr;
@@ -362,7 +365,7 @@ int main(int argc, char** argv) {
             double dms = 0, hms = 0, enc = 0;
             ABFT_TRY(abft_session_baseline(sess, 1, 0, &dms, &hms));
             ABFT_TRY(abft_session_encode(sess, &enc));
-            for (int f = 0; f < F; ++f) ABFT_TRY(abft_calibrate(ws, dC0, N_b, f, dDiff + fo[f], nullptr));
+            for (int f = 0; f < F; ++f) ABFT_TRY(abft_calibrate(ws, dC0, ldc, f, dDiff + fo[f], nullptr));
             CUDA_TRY(cudaMemcpy(hd.data(), dDiff, sizeof(double) * N_b, cudaMemcpyDeviceToHost));
             for (int j = 0; j < N_b; ++j) {
                 calib_diffs_local.push_back(hd[j]);
@@ -394,7 +397,8 @@ int main(int argc, char** argv) {
         if (record) base_samples.push_back(bhost / cfg.repeats);
         if (check_corrected && t == TOTAL - 1) {
             clean_c.resize((size_t)M_b * N_b);
-            CUDA_TRY(cudaMemcpy(clean_c.data(), dC0, sizeof(float) * clean_c.size(), cudaMemcpyDeviceToHost));
+            CUDA_TRY(cudaMemcpy2D(clean_c.data(), sizeof(float) * N_b, dC0, sizeof(float) * ldc, sizeof(float) * N_b,
+                                  M_b, cudaMemcpyDeviceToHost));
         }
         // Golden capture (main.cu:217-226). The reference uploads it to the
         // device only once (pipeline/passes.cuh:110-116), so only the first
@@ -402,7 +406,8 @@ int main(int argc, char** argv) {
         if (need_golden && !golden_set &&
             (cfg.reseed_per_trial || t == NUM_WARMUP - 1 || (NUM_WARMUP == 0 && t == 0))) {
             CUDA_TRY(cudaMalloc(&dG, sizeof(float) * (size_t)M_b * N_b));
-            CUDA_TRY(cudaMemcpy(dG, dC0, sizeof(float) * (size_t)M_b * N_b, cudaMemcpyDeviceToDevice));
+            CUDA_TRY(cudaMemcpy2D(dG, sizeof(float) * N_b, dC0, sizeof(float) * ldc, sizeof(float) * N_b, M_b,
+                                  cudaMemcpyDeviceToDevice));
             ABFT_TRY(abft_session_set_golden(sess, dG, N_b));
             golden_set = true;
         }
@@ -447,8 +452,8 @@ int main(int argc, char** argv) {
     if (check_corrected && !clean_c.empty()) {
         std::vector<float> fin(clean_c.size());
         for (int slot = 0; slot < std::min(cfg.repeats, 2); ++slot) {
-            CUDA_TRY(cudaMemcpy(fin.data(), slot == 0 ? dC0 : dC1, sizeof(float) * fin.size(),
-                                cudaMemcpyDeviceToHost));
+            CUDA_TRY(cudaMemcpy2D(fin.data(), sizeof(float) * N_b, slot == 0 ? dC0 : dC1, sizeof(float) * ldc,
+                                  sizeof(float) * N_b, M_b, cudaMemcpyDeviceToHost));
             for (size_t i = 0; i < fin.size(); ++i) {
                 const double g = clean_c[i];
                 const double d = std::fabs((double)fin[i] - g);

@@ -84,6 +84,15 @@ int abft_frag_count(int M, int K, int N, int M_b, int N_b, int frags_per_rank, i
     return F;
 }
 
+int64_t abft_c_pitch(int n) {
+    if (n < 1) {
+        set_error("abft_c_pitch: n must be >= 1");
+        return -1;
+    }
+    const int64_t bytes = 4 * (int64_t)n;
+    return (bytes % 65536 == 0) ? (int64_t)n + 32 : (int64_t)n;
+}
+
 // core/common.cuh:64-74
 double abft_matrix_inf_norm(const float* M, int rows, int cols, int64_t ld) {
     double mx = 0.0;

@@ -53,6 +53,17 @@ def frag_count(M, K, N, M_b, N_b, frags_per_rank=4, frag_cap=0):
     return F
 
 
+def c_pitch(n):
+    """Row pitch (floats) the sessions allocate for an n-column C: n, or
+    n + 32 when n * 4 bytes is a multiple of 64 KB (a fragment that is a
+    quarter of a 64 KB row streams ~9 % slower through the verify kernel
+    when every row starts at the same offset modulo 64 KB)."""
+    ld = lib.abft_c_pitch(int(n))
+    if ld < 1:
+        raise ValueError(f"bad column count {n}")
+    return int(ld)
+
+
 @dataclass
 class RankTile:
     """Geometry of one rank's tile on a Pr x Pc grid (main.cu:32-54)."""

@@ -34,7 +34,10 @@ class OnlineSession:
         self.offsets = np.ascontiguousarray(offsets, np.int32)
         self.F = len(self.counts)
         dev = self.A.device
-        self.C = [torch.empty((self.M_b, self.N_b), dtype=torch.float32, device=dev) for _ in range(2)]
+        # row pitch host.c_pitch(N_b): padded where a dense pitch would slow
+        # the verify kernel; C[i] is the M_b x N_b view of each buffer
+        ldc = host.c_pitch(self.N_b)
+        self.C = [torch.empty((self.M_b, ldc), dtype=torch.float32, device=dev)[:, :self.N_b] for _ in range(2)]
         self.golden = None
         self.max_iters = int(max_iters)
         cfg = SessionCfg()

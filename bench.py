@@ -587,7 +587,8 @@ def run_ours(args):
             "confusion_matrix": {"TP": int(cm_all[0]), "TN": int(cm_all[1]), "FP": int(cm_all[2]),
                                  "FN": int(cm_all[3]), "restored": int(cm_all[4])},
             "roofline": {
-                "kernel": f"fused verify (actualRow + detect), one {g.M_b}x{N_f} fragment (row pitch {g.N_b}) "
+                "kernel": f"fused verify (actualRow + detect), one {g.M_b}x{N_f} fragment "
+                          f"(row pitch {abft.c_pitch(g.N_b)}) "
                           "per launch",
                 "bound": "hbm", "achieved": iso_gbs, "peak": peak, "unit": "GB/s",
                 "frac": (iso_gbs / peak) if iso_gbs else None, "traffic": traffic,
@@ -631,11 +632,12 @@ def run_ours(args):
 
 # Fragment shapes (rows M_b, columns N_f, row pitch) of the workloads: F = 4
 # fragments of the rank tile: 1024^3 and 4096^3 on one GPU, the 16384^3
-# tiles at 1, 2, 4 and 8 GPUs, the 8192^3 2x4 tile, the non-square shapes,
+# tiles at 1, 2, 4 and 8 GPUs (at one GPU both the sessions' padded pitch,
+# 16416, and the dense 16384), the 8192^3 2x4 tile, the non-square shapes,
 # and a 1 GiB fragment.
-SWEEP_SHAPES = [(1024, 256, 1024), (4096, 1024, 4096), (16384, 4096, 16384), (16384, 2048, 8192),
-                (8192, 2048, 8192), (8192, 1024, 4096), (4096, 512, 2048), (16384, 256, 1024),
-                (1024, 4096, 16384), (65536, 4096, 4096)]
+SWEEP_SHAPES = [(1024, 256, 1024), (4096, 1024, 4096), (16384, 4096, 16416), (16384, 4096, 16384),
+                (16384, 2048, 8192), (8192, 2048, 8192), (8192, 1024, 4096), (4096, 512, 2048),
+                (16384, 256, 1024), (1024, 4096, 16384), (65536, 4096, 4096)]
 
 
 def verify_sweep(args):

@@ -64,6 +64,16 @@ int abft_choose_grid(int world, int* Pr, int* Pc);
 int abft_split_dim(int total, int parts, int* counts, int* offsets);
 /* Fragments per rank, main.cu:55-69 (small-matrix rule and --frag-cap). */
 int abft_frag_count(int M, int K, int N, int M_b, int N_b, int frags_per_rank, int64_t frag_cap);
+/* Row pitch (floats) for the pipeline's M_b x n row-major C buffers. The
+ * reference allocates C densely (ld = N_b, pipeline/buffers.cuh); here n gets
+ * 32 floats (128 B) more when n * 4 bytes is a multiple of 64 KB. With a 64 KB
+ * pitch every row of a fragment that is a quarter of the row starts at the
+ * same offset modulo 64 KB, and the verify kernel streams such a fragment
+ * about 9 % slower on B200 (59 us against 53.5 us for 16384 x 4096 of a
+ * 16384-wide C); the SGEMM's speed does not change. Any ldc >= n is valid
+ * for every entry point; this is only the layout the sessions and the driver
+ * allocate. Returns n unchanged otherwise; -1 for n < 1. */
+int64_t abft_c_pitch(int n);
 /* matrix_inf_norm, core/common.cuh:64-74 */
 double abft_matrix_inf_norm(const float* host_M, int rows, int cols, int64_t ld);
 /* compute_threshold_formula, core/common.cuh:77-83 */

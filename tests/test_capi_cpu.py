@@ -63,6 +63,16 @@ def test_frag_policy(abft):
     assert abft.frag_count(4096, 4096, 4096, 4096, 3, 4) == 3          # never more than N_b
 
 
+def test_c_pitch_pads_64k_multiples_only(abft):
+    # a dense 64 KB (or 128 KB ...) pitch gets 32 floats more; others stay dense
+    assert abft.c_pitch(16384) == 16416
+    assert abft.c_pitch(32768) == 32800
+    for n in (1, 256, 1000, 1024, 4096, 8192, 12288, 16385):
+        assert abft.c_pitch(n) == n
+    with pytest.raises(ValueError):
+        abft.c_pitch(0)
+
+
 def test_tile_injection_scheme_matches_oracle(abft, orc):
     """The tile-uniform scheme (seed 1 + iteration, (i, j) uniform over the tile)."""
     counts, offsets = abft.split_dim(1030, 3)

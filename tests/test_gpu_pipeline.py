@@ -103,6 +103,8 @@ def test_workload_shapes_normal_inputs(M, K, N, abft, orc):
     normal inputs, so the oracle replays every decision on the GPU's own C;
     counters, logs and final buffers must be bit-identical."""
     s, A, B, counts, offsets, tau, C0 = make_session(abft, orc, M, K, N, 4, dist="normal", max_iters=8)
+    # the wide tile's C rows are 64 KB: the session pads their pitch
+    assert s.C[0].stride(0) == abft.c_pitch(N) == (N + 32 if N == 16384 else N)
     assert tau[0] == 1e-5 * K * float(np.abs(A).max()) * float(np.abs(B).max())
     res = s.online("add", base_seed=11, repeats=4, log=True)
     o = orc.online_loop(C0, A, B, counts, offsets, tau, "add", "any", 1.0e6, 11, 0, 4)
