@@ -49,9 +49,8 @@ WsLayout ws_layout(int M_b, int N_b, int K, int F, int nfmax, int max_iters) {
     L.vd = take(sizeof(double) * nacc);
     L.vw = take(sizeof(double) * nacc);
     L.vcnt = take(sizeof(int) * vcnt_ints((int)groups));
-    L.lact = take(sizeof(double) * M_b);
-    L.ld = take(sizeof(double) * M_b);
-    L.lw = take(sizeof(double) * M_b);
+    L.lbd = take(sizeof(double) * M_b);
+    L.lbr = take(sizeof(int) * M_b);
     L.lcnt = take(sizeof(int) * 4);
     L.dlog = take(sizeof(DecisionLog) * (size_t)std::max(max_iters, 1) * F);
     L.ilog = take(sizeof(InjectLog) * (size_t)std::max(max_iters, 1));
@@ -174,9 +173,8 @@ int abft_ws_create(int M_b, int N_b, int K, int F, const int* counts, const int*
     d.vd = reinterpret_cast<double*>(b + L.vd);
     d.vw = reinterpret_cast<double*>(b + L.vw);
     d.vcnt = reinterpret_cast<int*>(b + L.vcnt);
-    d.lact = reinterpret_cast<double*>(b + L.lact);
-    d.ld = reinterpret_cast<double*>(b + L.ld);
-    d.lw = reinterpret_cast<double*>(b + L.lw);
+    d.lbd = reinterpret_cast<double*>(b + L.lbd);
+    d.lbr = reinterpret_cast<int*>(b + L.lbr);
     d.lcnt = reinterpret_cast<int*>(b + L.lcnt);
     d.dlog = reinterpret_cast<DecisionLog*>(b + L.dlog);
     d.ilog = reinterpret_cast<InjectLog*>(b + L.ilog);

@@ -86,9 +86,10 @@ struct WsDev {
     double* vd;
     double* vw;
     int* vcnt;         // [vcnt_ints(groups_max)], 8-byte aligned
-    double* lact;      // [M_b]
-    double* ld;
-    double* lw;
+    // localisation: per row block, its best row under the reference's
+    // arg-max order (-1: no row above tau) and that row's |actual - expected|
+    double* lbd;       // [M_b] (at most M_b / kWarps blocks)
+    int* lbr;          // [M_b]
     int* lcnt;         // [1]
     DecisionLog* dlog; // [max_iters][F]
     InjectLog* ilog;   // [max_iters]
@@ -117,7 +118,7 @@ void set_error(const std::string& msg);
 int cuda_fail(cudaError_t e, const char* what);
 
 struct WsLayout {
-    size_t colSumA, expRow, rowSumB, expCol, rec, ctr, vacc_s, vacc_t, vacc_m, vact, vd, vw, vcnt, lact, ld, lw, lcnt, dlog, ilog,
+    size_t colSumA, expRow, rowSumB, expCol, rec, ctr, vacc_s, vacc_t, vacc_m, vact, vd, vw, vcnt, lbd, lbr, lcnt, dlog, ilog,
         pend, plan, total;
 };
 WsLayout ws_layout(int M_b, int N_b, int K, int F, int nfmax, int max_iters);

@@ -294,6 +294,24 @@ struct SelectSmem {
     int flag;
 };
 
+// The order in which the reference's arg-max (k_detect_row / k_locate_correct,
+// kernels/abft_stepwise.cuh:85-110, :174-187) picks among entries above tau:
+// a strided scan keeps, per slot j % 256, the first strictly larger entry, and
+// a tree then lets the right operand (slot t + s against slot t) win only when
+// strictly larger. Among equal values the winner is the entry whose slot has
+// the smallest bit-reversed index (the tree's last level puts even slots before
+// odd ones, the one before it slots 0 mod 4 before 2 mod 4, ...), and within a
+// slot the smallest j. better() is that order as a comparison, so a reduction
+// in any order and grouping returns the reference's winner; j < 0 is "none".
+__device__ __forceinline__ bool sel_better(double da, int ja, double db, int jb) {
+    if (ja < 0) return false;
+    if (jb < 0) return true;
+    if (da != db) return da > db;
+    const unsigned ka = __brev((unsigned)ja & (kThreads - 1u)), kb = __brev((unsigned)jb & (kThreads - 1u));
+    if (ka != kb) return ka < kb;
+    return ja < jb;
+}
+
 // Loads of the arg-max inputs: CG = written by other CTAs of this grid (read
 // through L2), otherwise written by this CTA (shared or global memory).
 template <bool CG>
@@ -885,61 +903,128 @@ __device__ __forceinline__ void row_stats(const float* __restrict__ X, long long
     }
 }
 
+// |sum of a row in the reference's order - E|, for the rare uncertified
+// candidate row: kept out of line so that the streaming loop of the
+// localisation keeps its registers.
+__device__ __noinline__ double exact_row_diff(const float* __restrict__ row, int n, double E) {
+    return fabs(exact_chain(row, 1, n) - E);
+}
+
 // Gated localisation + correction for one fragment: row sums of the fragment
-// (a warp sums ROWS rows side by side), certified like the column sums, then the reference's row
-// arg-max (k_locate_correct) and the correction C = float(double(C) - rowdiff).
+// (a warp sums ROWS rows side by side), certified like the column sums, then
+// the reference's row arg-max (k_locate_correct) and the correction C =
+// float(double(C) - rowdiff). The arg-max is split across the grid: a row
+// whose fast sum could exceed tau but is not certified is re-summed in the
+// reference's order by the warp that summed it (its data is still in cache),
+// so every candidate value is exact; each CTA keeps its best row under the
+// reference's order (sel_better) and the last CTA reduces the per-CTA bests
+// (one entry per row block instead of one per row).
 template <bool VEC, int ROWS>
 __global__ void __launch_bounds__(kThreads)
     k_localize(float* C, long long ldc, int M, int N, int rows_per, int nblocks, const double* __restrict__ expc,
                double tau, int injected, const float* __restrict__ G, long long ldg, int frag_off, int f, int F,
                int it, int drain, int pend_cap, WsDev w, const InjectPlan* __restrict__ plan, int plan_it) {
-    __shared__ SelectSmem sel;
+    __shared__ double s_bd[kThreads];
+    __shared__ int s_bj[kThreads];
+    __shared__ int s_last;
     const int ec = __ldcg(&w.rec[f].errcol);
     if (ec < 0) return;
     if (plan != nullptr) injected = (plan[plan_it].frag == f) ? 1 : 0;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int r0 = blockIdx.x * rows_per;
     const int r1 = min(M, r0 + rows_per);
+    // this warp's best row so far, in shared memory (written by lane 0, read
+    // by the whole warp; rows above tau are rare)
+    if (lane == 0) {
+        s_bd[warp] = 0.0;
+        s_bj[warp] = -1;
+    }
+    __syncwarp();
     // ROWS rows per warp at a time, independent accumulators: their loads and
     // add chains overlap instead of paying one latency per row (narrow rows);
-    // a single row keeps 4 loads per lane in flight along the row instead.
+    // a single row keeps 8 loads per lane in flight along the row instead.
     for (int rb = r0 + warp; rb < r1; rb += ROWS * kWarps) {
+        // the expected sums first: their loads overlap the row's
+        double E[ROWS];
+#pragma unroll
+        for (int u = 0; u < ROWS; ++u) E[u] = (rb + u * kWarps < r1) ? expc[rb + u * kWarps] : 0.0;
         double s[ROWS];
         float t[ROWS];
         uint32_t m[ROWS];
         row_stats<VEC, ROWS>(C, ldc, N, rb, r1, s, t, m);
-        if (lane < ROWS) {
-            // lane u writes row u's results (a select keeps s, t, m in registers)
-            double su = s[0];
-            float tu = t[0];
-            uint32_t mu = m[0];
 #pragma unroll
-            for (int u = 1; u < ROWS; ++u)
-                if (lane == u) {
-                    su = s[u];
-                    tu = t[u];
-                    mu = m[u];
+        for (int u = 0; u < ROWS; ++u) {
+            const int r = rb + u * kWarps;
+            if (r < r1) {  // every lane holds the same statistics: warp-uniform branches
+                double d = fabs(s[u] - E[u]);
+                const double wv = cert_window(s[u], t[u], m[u], N, d);
+                if (wv != 0.0 && d + wv > tau) d = exact_row_diff(C + (long long)r * ldc, N, E[u]);
+                // the reference's scan takes entries above tau and above its
+                // initial 0
+                if (d > tau && d > 0.0 && sel_better(d, r, s_bd[warp], s_bj[warp])) {
+                    __syncwarp();
+                    if (lane == 0) {
+                        s_bd[warp] = d;
+                        s_bj[warp] = r;
+                    }
+                    __syncwarp();
                 }
-            const int r = rb + lane * kWarps;
-            if (r < r1) {
-                const double d = fabs(su - expc[r]);
-                w.lact[r] = su;
-                w.ld[r] = d;
-                w.lw[r] = cert_window(su, tu, mu, N, d);
             }
         }
     }
-    fence_acq_rel_gpu();
     __syncthreads();
-    if (tid == 0) sel.flag = (atomicAdd(w.lcnt, 1) == nblocks - 1);
+    if (tid == 0) {
+        double bd = s_bd[0];
+        int bj = s_bj[0];
+        for (int k = 1; k < kWarps; ++k)
+            if (sel_better(s_bd[k], s_bj[k], bd, bj)) {
+                bd = s_bd[k];
+                bj = s_bj[k];
+            }
+        w.lbd[blockIdx.x] = bd;
+        w.lbr[blockIdx.x] = bj;
+        fence_acq_rel_gpu();  // this block's best before its arrival
+        s_last = (atomicAdd(w.lcnt, 1) == nblocks - 1);
+    }
     __syncthreads();
-    if (!sel.flag) return;
+    if (!s_last) return;
     fence_acq_rel_gpu();
 
-    const int er = final_select<true>(
-        M, tau, expc, w.lact, w.ld, w.lw, [&](int i) { return exact_chain(C + (long long)i * ldc, 1, N); },
-        [](int) { return true; }, sel);
+    // Last CTA: the best of the per-block bests.
+    double bd = 0.0;
+    int bj = -1;
+    for (int b = tid; b < nblocks; b += kThreads) {
+        const int j = __ldcg(w.lbr + b);
+        if (j >= 0) {
+            const double d = __ldcg(w.lbd + b);
+            if (sel_better(d, j, bd, bj)) {
+                bd = d;
+                bj = j;
+            }
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const double od = __shfl_xor_sync(kFull, bd, o);
+        const int oj = __shfl_xor_sync(kFull, bj, o);
+        if (sel_better(od, oj, bd, bj)) {
+            bd = od;
+            bj = oj;
+        }
+    }
+    if (lane == 0) {
+        s_bd[warp] = bd;
+        s_bj[warp] = bj;
+    }
+    __syncthreads();
     if (tid == 0) {
+        int er = -1;
+        double be = 0.0;
+        for (int k = 0; k < kWarps; ++k)
+            if (sel_better(s_bd[k], s_bj[k], be, er)) {
+                be = s_bd[k];
+                er = s_bj[k];
+            }
         *w.lcnt = 0;
         const double rd = __ldcg(&w.rec[f].rowdiff);
         if (er >= 0) {

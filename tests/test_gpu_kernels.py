@@ -235,6 +235,27 @@ def test_exact_ties(abft, orc, torch_cuda):
         assert_same(g, o)
 
 
+@pytest.mark.parametrize("rows", [[5, 261], [261, 5], [64, 128], [128, 64, 517, 773], [1, 257, 513, 769, 1025],
+                                  [200, 100, 300], [1099, 0], [3, 10, 17, 24]])
+def test_exact_row_ties(rows, abft, orc, torch_cuda):
+    """Equal faults in several rows of one fragment (A = 0, so every faulty row
+    has exactly the same |actual - expected|): the localised row is decided by
+    the reference's scan-and-tree order alone - across row blocks, within one
+    slot (rows j and j + 256) and between slots (bit-reversed slot order)."""
+    M, K, N, F = 1100, 16, 1030, 2
+    A = np.zeros((M, K), np.float32)
+    _, B = tiles(orc, M, K, N)
+    counts, offsets = orc.split_dim(N, F)
+    C = np.zeros((M, N), np.float32)
+    for k, r in enumerate(rows):
+        C[r, 3 + 11 * k] = 3.0
+    tau = [0.5] * F
+    g = run_gpu_iteration(abft, torch_cuda, A, B, C, counts, offsets, tau, 0)
+    o = run_oracle_iteration(orc, A, B, C, counts, offsets, tau, 0)
+    assert_same(g, o)
+    assert o["er"][0] in rows
+
+
 def test_uncertified_sum_uses_sequential_value(abft, orc, torch_cuda):
     """Columns whose parallel double sum differs from the sequential one:
     2^30 followed by many 2^-27 terms. Each sequential add rounds the small
