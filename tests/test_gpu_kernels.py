@@ -235,6 +235,26 @@ def test_exact_ties(abft, orc, torch_cuda):
         assert_same(g, o)
 
 
+@pytest.mark.parametrize("row,col,fault", [(9700, 1234, "add"), (100, 4095, "add"), (7424, 7, "add"),
+                                           (9727, 2048, "flip"), (5000, 3000, "flip")])
+def test_verify_one_batch_tail_units(row, col, fault, abft, orc, torch_cuda):
+    """A fragment large enough that the verify schedule ends in one-batch
+    units (9728 x 4096: 18 CTAs per column group, each with at least four
+    128-row units, so rows from 7424 on are read in 64-row units): faults in
+    the bulk rows and in the tail rows are detected, located and corrected
+    exactly as by the oracle."""
+    M, K, N, F = 9728, 16, 4096, 1
+    A, B = tiles(orc, M, K, N, 31, 32)
+    counts, offsets = orc.split_dim(N, F)
+    C0 = product_f64(A, B)
+    C = add_fault(C0, row, col, 64.0) if fault == "add" else flip(C0, row, col, 30)
+    tau = [1.0]
+    g = run_gpu_iteration(abft, torch_cuda, A, B, C, counts, offsets, tau, 0)
+    o = run_oracle_iteration(orc, A, B, C, counts, offsets, tau, 0)
+    assert_same(g, o)
+    assert o["ec"][0] == col and o["er"][0] == row
+
+
 @pytest.mark.parametrize("rows", [[5, 261], [261, 5], [64, 128], [128, 64, 517, 773], [1, 257, 513, 769, 1025],
                                   [200, 100, 300], [1099, 0], [3, 10, 17, 24]])
 def test_exact_row_ties(rows, abft, orc, torch_cuda):
