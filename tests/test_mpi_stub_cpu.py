@@ -48,6 +48,17 @@ def free_base(n):
 
 
 def launch(binary, world, extra_env=None):
+    """Runs world ranks; a run in which a rank could not bind its port (taken
+    by another process between the check and the bind) is retried on a new
+    port range, up to three times."""
+    for attempt in range(3):
+        outs = launch_once(binary, world, extra_env)
+        if not any("bind to port" in e for _, _, e in outs):
+            break
+    return outs
+
+
+def launch_once(binary, world, extra_env=None):
     base = free_base(world)
     procs = []
     for r in range(world):
